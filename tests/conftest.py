@@ -1,0 +1,24 @@
+"""Shared test setup: the `gpu` marker, import paths and small helpers.
+
+Tests marked `gpu` need a CUDA device and the built library; everything else runs on CPU.
+"""
+import os
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+for p in (ROOT, ROOT / "vllm-exact_b200", ROOT / "tests" / "golden"):
+    if str(p) not in sys.path:
+        sys.path.insert(0, str(p))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200) and the built sm_100a library")
+
+
+@pytest.fixture(scope="session")
+def golden():
+    import json
+    return json.loads((ROOT / "tests" / "golden" / "golden.json").read_text())
