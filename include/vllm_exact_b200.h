@@ -1,0 +1,153 @@
+/*
+ * vllm-exact B200 library: C ABI of the two hot paths of vllm-exact, built for sm_100a.
+ *
+ *   1. exact_int8 linear layer: fixed-point digitization + exact two-digit integer GEMM with fused epilogue;
+ *   2. batch-invariant paged decode attention.
+ *
+ * Conventions (all entry points):
+ *   - every pointer is caller-owned device memory; nothing here allocates device memory;
+ *   - every call is asynchronous and stream-ordered on `stream` (a cudaStream_t; NULL = legacy default stream);
+ *     no entry point synchronizes the host;
+ *   - the return value is EX_OK or an EX_ERR_* status; bad arguments are reported before anything is launched;
+ *   - strides / leading dimensions are in ELEMENTS of the tensor they describe;
+ *   - split-K workspaces must be zero-filled once before first use; each call leaves them zero again.
+ *     Calls that share a workspace must not overlap on the GPU (use one workspace per stream).
+ *
+ * Each entry point names the reference function it replaces (catoneone/vllm-exact, path:line).
+ */
+#ifndef VLLM_EXACT_B200_H
+#define VLLM_EXACT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+enum {
+  EX_OK = 0,
+  EX_ERR_ARG = 1,         /* bad shape, mode or null pointer */
+  EX_ERR_ALIGN = 2,       /* pointer or leading dimension not aligned as the chosen kernel requires */
+  EX_ERR_WORKSPACE = 3,   /* workspace missing or smaller than the *_workspace_bytes() answer */
+  EX_ERR_DTYPE = 4,       /* unsupported element type */
+  EX_ERR_UNSUPPORTED = 5, /* requested algorithm cannot run this shape on this device */
+  EX_ERR_CUDA = 6,        /* CUDA runtime error at launch; see ex_last_error_string() */
+  EX_ERR_DEVICE = 7       /* a kernel reported a bounded wait that timed out (see ex_device_error) */
+};
+
+/* element types */
+enum { EX_DTYPE_F32 = 0, EX_DTYPE_BF16 = 1, EX_DTYPE_F16 = 2 };
+
+/* exact GEMM algorithms; all produce bit-identical results */
+enum {
+  EX_ALGO_AUTO = 0,    /* pick by shape */
+  EX_ALGO_SIMT = 1,    /* CUDA cores, int8 dp4a, int32 accumulation */
+  EX_ALGO_TC_I8 = 2,   /* tcgen05 kind::i8 tensor cores, TMA-fed, int32 accumulators in tensor memory */
+  EX_ALGO_TC_BF16 = 3  /* tcgen05 kind::f16 tensor cores on bf16-converted digits, fp32 accumulators drained to int */
+};
+
+const char* ex_version(void);
+const char* ex_status_string(int status);
+/* Message of the last EX_ERR_CUDA on this host thread. */
+const char* ex_last_error_string(void);
+
+/* Synchronizes the current device, stores the device error word into *code (0 = none) and clears it.
+ * Returns EX_OK, or EX_ERR_CUDA if the synchronize failed. For tests and diagnostics, not for hot paths. */
+int ex_device_error(int* code);
+
+/*
+ * Per-row fixed-point digitization.
+ * Replaces kernels.digitize / _digitize_kernel (src/vllm_exact/kernels.py:74-85, :46-71), with the semantics of
+ * digitize_torch (kernels.py:22-39): per row a = max|x|, e = frexp exponent of a (0 if a == 0), sh = F - e,
+ * q = trunc(x * 2^sh); F = 14 balanced digits (cs = 0), F = 15 offset digits with row sum cs.
+ *   x      rows x K, element type x_dtype (EX_DTYPE_F32/BF16/F16), leading dimension ldx
+ *   h, l   rows x K int8 digits, leading dimension ldd (>= K)
+ *   cs, sh rows int32
+ */
+int ex_digitize(const void* x, int x_dtype, int64_t ldx, int64_t rows, int64_t K, int F, int8_t* h, int8_t* l,
+                int64_t ldd, int32_t* cs, int32_t* sh, void* stream);
+
+/*
+ * Row maxima for tensor-parallel digitization: amax[r] = max_k |x[r, k]| (float32; exact).
+ * No reference counterpart: the reference runs on one GPU. A K-sharded (row-parallel) layer needs the row scale of
+ * the WHOLE row (src/vllm_exact/kernels.py:25-29 computes it from the whole row), so each rank computes the maxima of
+ * its K slice, the ranks take the elementwise MAX (an exact, order-free all-reduce), and the slice is digitized with
+ * ex_digitize_given_absmax.
+ */
+int ex_row_absmax(const void* x, int x_dtype, int64_t ldx, int64_t rows, int64_t K, float* amax, void* stream);
+
+/*
+ * ex_digitize with the per-row maximum supplied by the caller (amax[r] >= max_k |x[r, k]|, e.g. the all-reduced
+ * maximum over all K shards): the digits of a K slice are then exactly the corresponding slice of the digits of the
+ * whole row (semantics of digitize_torch, src/vllm_exact/kernels.py:22-39, with `a` taken from amax). For F = 15, cs
+ * is the row sum over this slice only; slice sums add up to the whole row's sum.
+ */
+int ex_digitize_given_absmax(const void* x, int x_dtype, int64_t ldx, int64_t rows, int64_t K, int F,
+                             const float* amax, int8_t* h, int8_t* l, int64_t ldd, int32_t* cs, int32_t* sh,
+                             void* stream);
+
+/* Bytes of zero-initialised split-K workspace that ex_linear / ex_linear_partial_i64 need for this shape, split_k
+ * (0 = automatic) and algorithm. 0 means no workspace is needed. */
+size_t ex_linear_workspace_bytes(int64_t M, int64_t N, int64_t K, int split_k, int algo);
+
+/*
+ * Exact linear layer: out (M x N) = fp32(fp64(tot) * 2^-(sx+sw)) rounded to out_dtype, where
+ * tot = 2^16 xh.wh + 2^8 (xh.wl + xl.wh) [+ xl.wl unless trunc] [+ 128 (cx + cw) + 2^14 K when F == 15].
+ * Replaces kernels.exact_linear (src/vllm_exact/kernels.py:257-289) with its kernels _exact_kernel (:103-157),
+ * _exact_bf16_kernel (:180-247) and _exact_fin (:159-177). Bit-identical to exact_linear_torch (:89-100) for every
+ * algorithm and split_k.
+ *   xh, xl (M x K, ld ldx) activation digits; cx, sx (M) int32;   wh, wl (N x K, ld ldw) weight digits; cw, sw (N)
+ *   cx / cw are read only when F == 15 (may be NULL otherwise)
+ *   split_k: 0 = automatic, >= 1 = number of K partitions (results are identical for every value)
+ */
+int ex_linear(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* cx, const int32_t* sx,
+              const int8_t* wh, const int8_t* wl, int64_t ldw, const int32_t* cw, const int32_t* sw, int64_t M,
+              int64_t N, int64_t K, int F, int trunc, void* out, int out_dtype, int64_t ldo, void* workspace,
+              size_t workspace_bytes, int split_k, int algo, void* stream);
+
+/*
+ * Integer part of ex_linear without the scaling epilogue: tot (M x N int64, ld ldt) = the exact integer total
+ * of this K slice, including the F == 15 offset terms of the slice. Summing the tot of disjoint K slices (e.g. an
+ * int64 all-reduce over K-sharded ranks) gives exactly the tot of the whole K range. This is the row-parallel
+ * (K-sharded) building block; the reference has it only inside the split-K plumbing (kernels.py:144-146, :271-273).
+ */
+int ex_linear_partial_i64(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* cx, const int8_t* wh,
+                          const int8_t* wl, int64_t ldw, const int32_t* cw, int64_t M, int64_t N, int64_t K, int F,
+                          int trunc, int64_t* tot, int64_t ldt, void* workspace, size_t workspace_bytes, int split_k,
+                          int algo, void* stream);
+
+/*
+ * Scaling epilogue of an int64 total: out = fp32(fp64(tot) * 2^-(sx+sw)) rounded to out_dtype.
+ * Replaces the epilogue of _exact_fin (src/vllm_exact/kernels.py:172-177).
+ */
+int ex_epilogue_i64(const int64_t* tot, int64_t ldt, const int32_t* sx, const int32_t* sw, int64_t M, int64_t N,
+                    void* out, int out_dtype, int64_t ldo, void* stream);
+
+/* Bytes of (uninitialised) partial-result workspace ex_paged_decode needs. */
+size_t ex_paged_decode_workspace_bytes(int n, int H, int D, int max_len, int split);
+
+/*
+ * Batch-invariant paged decode attention over a paged KV cache.
+ * Replaces paged_attn.paged_decode with _paged_partial / _paged_merge (src/vllm_exact/paged_attn.py:97-114,
+ * :31-94). For each request b < n and query head h (KV head h / (H/KV)): softmax(scale * q.K^T) V over the first
+ * seq_lens[b] tokens, token t at page block_table[b, t / BS], offset t % BS. Each request's keys are processed in
+ * fixed segments of `split` keys (NS = ceil(max_len / split) segments) merged in fixed order, so a request's output
+ * bits do not depend on n, on the other requests, or on where its pages are placed.
+ *   q        (>= n) x H x D, strides (sq_t, sq_h, 1), bf16
+ *   k_cache, v_cache: num_blocks x BS x KV x D with strides (s_block, s_page, s_head, 1), bf16
+ *   block_table int32 (n x pages, row stride sbt); seq_lens int32 (n)
+ *   out      (>= n) x H x D, strides (so_t, so_h, 1), out_dtype (bf16, fp16 or fp32)
+ */
+int ex_paged_decode(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cache, const void* v_cache,
+                    int64_t s_block, int64_t s_page, int64_t s_head, const int32_t* block_table, int64_t sbt,
+                    const int32_t* seq_lens, int n, int H, int KV, int D, int BS, float scale, int max_len, int split,
+                    void* out, int64_t so_t, int64_t so_h, int out_dtype, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VLLM_EXACT_B200_H */

@@ -38,19 +38,23 @@ def _frexp_exponent(a: np.ndarray) -> np.ndarray:
     return np.where(a > 0, e, 0).astype(np.int32)
 
 
-def digitize(x: np.ndarray, F: int):
+def digitize(x: np.ndarray, F: int, amax: np.ndarray | None = None):
     """(R, K) float -> (h int8, l int8, cs int32, sh int32), bit for bit like digitize_torch (kernels.py:22-39).
 
     Per row: a = max|x|, e = frexp exponent of a (0 for an all-zero row), sh = F - e, scale = 2^sh built from float32
     bits with int32 wrap-around exactly as the reference does ((sh + 127) << 23, kernels.py:29), q = trunc(x * scale)
     toward zero (kernels.py:30). F = 14: balanced digits l = ((q + 128) & 255) - 128, h = (q - l) >> 8, cs = 0
     (kernels.py:36-38). F = 15: offset digits l = (q & 255) - 128, h = (q - l - 128) >> 8 and the row sum
-    cs = sum(256 h + l) (kernels.py:32-34).
+    cs = sum(256 h + l) (kernels.py:32-34). With `amax` given, a is taken from it instead of from the row itself (the
+    digits of a K slice are then the matching slice of the whole row's digits).
     """
     if F not in (14, 15):
         raise ValueError("F must be 14 or 15")
     x = np.ascontiguousarray(x, dtype=np.float32)
-    a = np.abs(x).max(axis=1) if x.shape[1] else np.zeros(x.shape[0], np.float32)
+    if amax is not None:  # row maximum supplied (tensor parallelism: the maximum over every K shard of the row)
+        a = np.asarray(amax, dtype=np.float32)
+    else:
+        a = np.abs(x).max(axis=1) if x.shape[1] else np.zeros(x.shape[0], np.float32)
     e = _frexp_exponent(a)
     sh = (F - e).astype(np.int32)
     bits = ((sh.astype(np.int64) + 127) << 23).astype(np.uint64) & np.uint64(0xFFFFFFFF)  # int32 wrap-around

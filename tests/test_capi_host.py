@@ -1,0 +1,71 @@
+"""CPU tests of the C-ABI library: it loads without a GPU, exports every symbol the header declares, and rejects bad
+arguments with the documented status codes before touching the device (no compute call runs here)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "vllm_exact_b200.h"
+
+
+@pytest.fixture(scope="module")
+def L():
+    from vllm_exact import _lib
+    if not _lib.LIB_PATH.exists():
+        pytest.skip("library not built")
+    return _lib.lib()
+
+
+def _declared():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\*?\s+\*?(ex_[a-z_0-9]+)\(", text, re.M)))
+
+
+def test_header_symbols_exported(L):
+    from vllm_exact import _lib
+    names = _declared()
+    assert len(names) >= 11
+    for n in names:
+        assert hasattr(L, n), n
+    assert set(names) == set(_lib.SIGNATURES), "ctypes signatures must cover exactly the header's entry points"
+
+
+def test_version_and_status_strings(L):
+    assert b"sm_100a" in L.ex_version()
+    assert L.ex_status_string(0) == b"ok"
+    assert L.ex_status_string(3).startswith(b"workspace")
+
+
+def test_argument_validation_without_gpu(L):
+    from vllm_exact import _lib as X
+    p = ctypes.c_void_p(16)  # never dereferenced: every call below must fail validation first
+    # digitize: bad F, bad dtype, negative rows
+    assert L.ex_digitize(p, 1, 64, 4, 64, 13, p, p, 64, p, p, None) == X.EX_ERR_ARG
+    assert L.ex_digitize(p, 9, 64, 4, 64, 14, p, p, 64, p, p, None) == X.EX_ERR_DTYPE
+    assert L.ex_digitize(p, 1, 64, -1, 64, 14, p, p, 64, p, p, None) == X.EX_ERR_ARG
+    assert L.ex_digitize(p, 1, 32, 4, 64, 14, p, p, 64, p, p, None) == X.EX_ERR_ARG  # ldx < K
+    assert L.ex_digitize(None, 1, 64, 0, 64, 14, None, None, 64, None, None, None) == X.EX_OK  # empty
+    # linear: K beyond the int32-exact range, bad F, bad out dtype, ldo < N
+    args = lambda M, N, K, F, od, ldo: (p, p, K, p, p, p, p, K, p, p, M, N, K, F, 1, p, od, ldo, None, 0, 0, 0, None)
+    assert L.ex_linear(*args(4, 8, 1 << 17, 14, 1, 8)) == X.EX_ERR_UNSUPPORTED
+    assert L.ex_linear(*args(4, 8, 64, 16, 1, 8)) == X.EX_ERR_ARG
+    assert L.ex_linear(*args(4, 8, 64, 14, 7, 8)) == X.EX_ERR_DTYPE
+    assert L.ex_linear(*args(4, 8, 64, 14, 1, 4)) == X.EX_ERR_ARG
+    assert L.ex_linear(*args(0, 8, 64, 14, 1, 8)) == X.EX_OK  # empty batch is a no-op
+    # split-K needs a workspace: SIMT with 4 splits, none given
+    a = list(args(4, 8, 4096, 14, 1, 8))
+    a[20], a[21] = 4, X.EX_ALGO_SIMT
+    assert L.ex_linear(*a) == X.EX_ERR_WORKSPACE
+    assert L.ex_linear_workspace_bytes(4, 8, 4096, 4, X.EX_ALGO_SIMT) >= 4 * 8 * 8
+    assert L.ex_linear_workspace_bytes(4, 8, 4096, 1, X.EX_ALGO_SIMT) == 0
+    # epilogue / paged decode
+    assert L.ex_epilogue_i64(p, 4, p, p, 4, 8, p, 1, 8, None) == X.EX_ERR_ARG
+    pd = lambda H, KV, D, ws, wsb: (p, 64, 32, ctypes.c_void_p(256), ctypes.c_void_p(256), 64, 64, 64, p, 4, p, 2, H,
+                                   KV, D, 16, 0.1, 4096, 4096, p, 64, 32, 1, ws, wsb, None)
+    assert L.ex_paged_decode(*pd(32, 6, 128, None, 0)) == X.EX_ERR_ARG      # H % KV != 0
+    assert L.ex_paged_decode(*pd(32, 8, 96, None, 0)) == X.EX_ERR_UNSUPPORTED  # head size
+    assert L.ex_paged_decode(*pd(64, 2, 128, None, 0)) == X.EX_ERR_UNSUPPORTED  # 32 query heads per KV head
+    assert L.ex_paged_decode(*pd(32, 8, 128, None, 0)) == X.EX_ERR_WORKSPACE
+    assert L.ex_paged_decode_workspace_bytes(2, 32, 128, 4096, 4096) >= 2 * 32 * (128 + 2) * 4

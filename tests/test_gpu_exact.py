@@ -1,0 +1,193 @@
+"""GPU parity tests of the exact_int8 linear path: every algorithm and split-K factor of the sm_100a library must be
+bitwise identical to the CPU oracle (which is pinned to the reference's own CPU path by golden hashes).
+
+Follows the reference's tests/test_gpu.py:13-43 (shapes, extreme-digit fixture, bf16 = fp32-then-bf16 rounding,
+bf16 / fp32 digitizer inputs) and adds config 1, odd shapes, batch-invariance and K-slice properties."""
+import numpy as np
+import pytest
+import torch
+
+import recipes as R
+from oracle import exact_oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+ALGOS = ["simt", "tc_i8"]
+
+
+@pytest.fixture(scope="module")
+def K():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    from vllm_exact import kernels
+    return kernels
+
+
+def _algo(K, name):
+    return {"simt": K.EX_ALGO_SIMT, "tc_i8": K.EX_ALGO_TC_I8, "auto": K.EX_ALGO_AUTO}[name]
+
+
+def _np(t):
+    t = t.detach().cpu()
+    return t.float().numpy() if t.dtype == torch.bfloat16 else t.numpy()
+
+
+def _digits_np(xd):
+    return [_np(t) for t in xd]
+
+
+def _run(K, xd, wd, F, tr, algo, sk, dtype=torch.float32):
+    M, N = xd[0].shape[0], wd[0].shape[0]
+    out = torch.empty(M, N, device=DEV, dtype=dtype)
+    K.exact_linear(xd, wd, F, tr, out=out, cfg={"algo": _algo(K, algo), "split_k": sk})
+    return out
+
+
+def test_config1_golden_bf16(K, golden):
+    """bf16 output hashes to the reference's golden sha256 for every algorithm and split."""
+    x, w = R.config1()
+    xd, wd = K.digitize(x.to(DEV), 14), K.digitize(w.to(DEV), 14)
+    assert [R.sha(t.cpu().contiguous()) for t in xd] == golden["config1"]["xd_sha"]
+    assert [R.sha(t.cpu().contiguous()) for t in wd] == golden["config1"]["wd_sha"]
+    for algo in ALGOS:
+        for sk in (0, 1, 2, 4, 8):
+            y = _run(K, xd, wd, 14, True, algo, sk, torch.bfloat16)
+            assert R.sha(y) == golden["config1"]["y_bf16_sha"], (algo, sk)
+
+
+@pytest.mark.parametrize("idx", range(8))
+def test_reference_shapes_bitwise(K, golden, idx):
+    """Reference tests/test_gpu.py:13-32: every algorithm and split-K factor equals the CPU integer result; bf16 output
+    equals the fp32 result rounded to bf16."""
+    c = golden["extreme_digit_cases"][idx]
+    F, tr = c["F"], c["trunc"]
+    x, w = R.extreme_digits(c["M"], c["N"], c["K"])
+    xd, wd = K.digitize(x.to(DEV), F), K.digitize(w.to(DEV), F)
+    assert [R.sha(t.cpu().contiguous()) for t in xd] == c["xd_sha"]
+    assert [R.sha(t.cpu().contiguous()) for t in wd] == c["wd_sha"]
+    ref = O.exact_linear(_digits_np(xd), _digits_np(wd), F, tr)
+    assert R.sha(ref) == c["y_f32_sha"]
+    ref_b = O.f32_to_bf16_bits(ref)
+    for algo in ALGOS:
+        for sk in (0, 1, 2, 4, 8):
+            y = _run(K, xd, wd, F, tr, algo, sk)
+            assert np.array_equal(_np(y).view(np.uint32), ref.view(np.uint32)), (algo, sk)
+            yb = _run(K, xd, wd, F, tr, algo, sk, torch.bfloat16)
+            assert np.array_equal(yb.cpu().view(torch.int16).numpy().view(np.uint16), ref_b), (algo, sk)
+
+
+@pytest.mark.parametrize("F", [14, 15])
+def test_digitize_inputs_match_oracle(K, golden, F):
+    """Reference tests/test_gpu.py:35-43: bf16 input == fp32 input == CPU digitizer; plus the edge rows (zero row,
+    subnormal maxima, largest bf16, ...) pinned by the reference's own outputs."""
+    xb = R.digitize_bf16_input()
+    a = K.digitize(xb.to(DEV), F)
+    b = K.digitize(xb.float().to(DEV), F)
+    for u, v in zip(a, b):
+        assert torch.equal(u, v)
+    assert [R.sha(t.cpu().contiguous()) for t in a] == golden["digitize_bf16"]["out"][str(F)]
+    xe = R.digitize_edge_rows()
+    e = K.digitize(xe.to(DEV), F)
+    assert [int(v) for v in e[3].cpu()] == golden["digitize_edge"]["sh"][str(F)]
+    assert [R.sha(t.cpu().contiguous()) for t in e] == golden["digitize_edge"]["out"][str(F)]
+    e16 = K.digitize(xe.bfloat16().to(DEV), F)
+    for u, v in zip(e, e16):
+        assert torch.equal(u, v)
+
+
+@pytest.mark.parametrize("M,N,Kd", [(1, 64, 4096), (3, 130, 1000), (17, 257, 784), (64, 384, 2048),
+                                    (130, 640, 1536), (1, 1, 16), (7, 33, 512)])
+@pytest.mark.parametrize("F,tr", [(14, True), (15, False), (14, False), (15, True)])
+def test_odd_shapes_all_modes(K, M, N, Kd, F, tr):
+    """Ragged M/N/K tails (K not a multiple of the 128-byte tile, N not a multiple of 128, token tails) and all four
+    (F, trunc) modes, against the oracle."""
+    g = torch.Generator().manual_seed(M * 1000 + N + Kd)
+    x = torch.randn(M, Kd, generator=g)
+    x[:, min(7, Kd - 1)] *= 300
+    w = torch.randn(N, Kd, generator=g) * 0.02
+    w[:, min(3, Kd - 1)] *= 300
+    xd, wd = K.digitize(x.to(DEV), F), K.digitize(w.to(DEV), F)
+    ref = O.exact_linear(_digits_np(xd), _digits_np(wd), F, tr)
+    for algo in ALGOS:
+        for sk in (0, 1, 3):
+            y = _run(K, xd, wd, F, tr, algo, sk)
+            assert np.array_equal(_np(y).view(np.uint32), ref.view(np.uint32)), (algo, sk)
+
+
+def test_unaligned_leading_dimension_uses_simt(K):
+    """Digits whose rows are not 16-byte aligned cannot be TMA-loaded: AUTO falls back to the SIMT kernel (same bits)
+    and an explicit tensor-core request is refused with EX_ERR_ALIGN."""
+    from vllm_exact import _lib
+    M, N, Kd = 5, 70, 100
+    g = torch.Generator().manual_seed(3)
+    x, w = torch.randn(M, Kd, generator=g), torch.randn(N, Kd, generator=g) * 0.02
+    xd = [t.to(DEV) for t in (torch.from_numpy(v) for v in O.digitize(x.numpy(), 14))]
+    wd = [t.to(DEV) for t in (torch.from_numpy(v) for v in O.digitize(w.numpy(), 14))]
+    assert xd[0].stride(0) == 100
+    ref = O.exact_linear(_digits_np(xd), _digits_np(wd), 14, True)
+    y = _run(K, xd, wd, 14, True, "auto", 0)
+    assert np.array_equal(_np(y).view(np.uint32), ref.view(np.uint32))
+    with pytest.raises(_lib.ExactError) as ei:
+        _run(K, xd, wd, 14, True, "tc_i8", 0)
+    assert ei.value.status == _lib.EX_ERR_ALIGN
+
+
+def test_batch_invariance_rows(K):
+    """Config 3 in small: 16 fixed target rows embedded at random positions in batches of many sizes, every split
+    and algorithm: each target row's output bits never change (reference tests/test_reference_cpu.py:37-46)."""
+    Kd, N = 12288, 512
+    g = torch.Generator().manual_seed(0)
+    targets = torch.randn(16, Kd, generator=g)
+    w = torch.randn(N, Kd, generator=torch.Generator().manual_seed(1)) * 0.02
+    wd = K.digitize(w.to(DEV), 14)
+    base = _run(K, K.digitize(targets.to(DEV), 14), wd, 14, True, "simt", 1, torch.bfloat16)
+    for M in (1, 2, 7, 16, 33, 64, 100, 256):
+        gm = torch.Generator().manual_seed(M)
+        filler = torch.randn(M, Kd, generator=gm)
+        filler[torch.rand(M, Kd, generator=gm) < 0.001] *= 50
+        nt = min(M, 16)
+        pos = torch.randperm(M, generator=gm)[:nt]
+        filler[pos] = targets[:nt]
+        xd = K.digitize(filler.to(DEV), 14)
+        for algo in ALGOS:
+            for sk in (0, 1, 2, 4, 8):
+                y = _run(K, xd, wd, 14, True, algo, sk, torch.bfloat16)
+                assert torch.equal(y[pos.to(DEV)], base[:nt]), (M, algo, sk)
+
+
+def test_k_slices_sum_exactly(K):
+    """Row-parallel building block: int64 totals of disjoint K slices add up to the total of the whole K range, and
+    the separate epilogue reproduces exact_linear (reference tests/test_reference_cpu.py:49-60)."""
+    M, N, Kd = 24, 384, 4096
+    x, w = R.extreme_digits(M, N, Kd)
+    for F, tr in ((14, True), (15, False)):
+        xd, wd = K.digitize(x.to(DEV), F), K.digitize(w.to(DEV), F)
+        full = K.exact_linear_partial_i64(xd, wd, F, tr)
+        ref = O.exact_linear_i64(_digits_np(xd), _digits_np(wd), F, tr)
+        assert np.array_equal(full.cpu().numpy(), ref)
+        tot = torch.zeros_like(full)
+        for a, b in ((0, 1024), (1024, 3072), (3072, 4096)):
+            # a K slice of the digits: row sums of the slice for F = 15, same row shifts
+            xs = [xd[0][:, a:b], xd[1][:, a:b]]
+            ws = [wd[0][:, a:b], wd[1][:, a:b]]
+            if F == 15:
+                cxs = (256 * xs[0].long() + xs[1].long()).sum(1).to(torch.int32)
+                cws = (256 * ws[0].long() + ws[1].long()).sum(1).to(torch.int32)
+            else:
+                cxs, cws = torch.zeros_like(xd[2]), torch.zeros_like(wd[2])
+            for algo in ALGOS:
+                part = K.exact_linear_partial_i64([*xs, cxs, xd[3]], [*ws, cws, wd[3]], F, tr,
+                                                  cfg={"algo": _algo(K, algo), "split_k": 2})
+                if algo == ALGOS[0]:
+                    tot += part
+                else:
+                    assert torch.equal(part, K.exact_linear_partial_i64([*xs, cxs, xd[3]], [*ws, cws, wd[3]], F, tr,
+                                                                        cfg={"algo": _algo(K, ALGOS[0])}))
+        assert torch.equal(tot, full)
+        y = K.exact_epilogue(tot, xd[3], wd[3], torch.empty(M, N, device=DEV, dtype=torch.bfloat16))
+        assert torch.equal(y, K.exact_linear(xd, wd, F, tr, out=torch.empty_like(y)))
+
+
+def test_no_device_timeouts(K):
+    from vllm_exact import _lib
+    assert _lib.device_error() == 0

@@ -1,0 +1,342 @@
+// C ABI of the vllm-exact B200 library (declarations and contracts: include/vllm_exact_b200.h).
+//
+// The whole library is one translation unit (this file includes the kernel headers) so that every kernel shares the
+// single device error word g_ex_dev_error. Every entry point validates its arguments before launching anything,
+// never allocates device memory and never synchronizes the host.
+#include <string>
+
+#include "ex_common.cuh"
+#include "ex_digitize.cuh"
+#include "ex_gemm_simt.cuh"
+#include "ex_gemm_tc.cuh"
+#include "ex_paged_decode.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return EX_OK;
+  g_last_error = cudaGetErrorString(e);
+  return EX_ERR_CUDA;
+}
+
+bool dtype_ok(int d) { return d == EX_DTYPE_F32 || d == EX_DTYPE_BF16 || d == EX_DTYPE_F16; }
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+int num_sms() {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+      sms = v;
+    else
+      sms = 148;
+  }
+  return sms;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// SIMT plan: row blocks of 256 weight rows, K split so that there are about two CTAs per SM.
+// ---------------------------------------------------------------------------------------------------------------
+struct SimtPlan {
+  int splits;
+  int kchunk;
+  int nblocks;
+  size_t ws_bytes;
+};
+
+SimtPlan simt_plan(int64_t M, int64_t N, int64_t K, int split_k) {
+  SimtPlan p;
+  p.nblocks = (int)cdiv(N, ex::SIMT_THREADS);
+  int s = split_k;
+  if (s <= 0) {
+    const int target = 2 * num_sms();
+    s = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(target, p.nblocks), K / 256));
+  }
+  s = (int)std::max<int64_t>(1, std::min<int64_t>(s, std::max<int64_t>(1, cdiv(K, 16))));
+  p.kchunk = (int)std::max<int64_t>(16, align_up((size_t)cdiv(K, s), 16));
+  p.splits = K > 0 ? (int)cdiv(K, p.kchunk) : 1;
+  p.ws_bytes = p.splits > 1 ? align_up((size_t)p.nblocks * 4, 256) + (size_t)M * N * 8 : 0;
+  return p;
+}
+
+template <int F, bool TRUNC, int OD, bool PARTIAL>
+cudaError_t launch_simt_t(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* cx, const int32_t* sx,
+                          const int8_t* wh, const int8_t* wl, int64_t ldw, const int32_t* cw, const int32_t* sw,
+                          int M, int N, int K, const SimtPlan& p, void* out, int64_t ldo, void* ws, cudaStream_t st) {
+  const bool vecw = (ldw % 16 == 0) && (reinterpret_cast<uintptr_t>(wh) % 16 == 0) &&
+                    (reinterpret_cast<uintptr_t>(wl) % 16 == 0);
+  int* cnt = reinterpret_cast<int*>(ws);
+  long long* acc = p.splits > 1 ? reinterpret_cast<long long*>(reinterpret_cast<char*>(ws) +
+                                                               align_up((size_t)p.nblocks * 4, 256))
+                                 : nullptr;
+  dim3 grid(p.nblocks, p.splits);
+  ex::k_exact_simt<F, TRUNC, OD, PARTIAL><<<grid, ex::SIMT_THREADS, 0, st>>>(
+      xh, xl, ldx, cx, sx, wh, wl, ldw, cw, sw, M, N, K, p.kchunk, vecw, out, ldo, acc, cnt);
+  return cudaGetLastError();
+}
+
+template <bool PARTIAL>
+cudaError_t launch_simt(int F, int trunc, int od, const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* cx,
+                        const int32_t* sx, const int8_t* wh, const int8_t* wl, int64_t ldw, const int32_t* cw,
+                        const int32_t* sw, int M, int N, int K, const SimtPlan& p, void* out, int64_t ldo, void* ws,
+                        cudaStream_t st) {
+#define EX_SIMT_CASE(FF, TT, OO)                                                                              \
+  if (F == FF && (trunc != 0) == TT && (PARTIAL || od == OO))                                                 \
+    return launch_simt_t<FF, TT, OO, PARTIAL>(xh, xl, ldx, cx, sx, wh, wl, ldw, cw, sw, M, N, K, p, out, ldo, \
+                                              ws, st);
+  EX_SIMT_CASE(14, true, EX_DTYPE_BF16)
+  EX_SIMT_CASE(14, true, EX_DTYPE_F32)
+  EX_SIMT_CASE(14, true, EX_DTYPE_F16)
+  EX_SIMT_CASE(14, false, EX_DTYPE_BF16)
+  EX_SIMT_CASE(14, false, EX_DTYPE_F32)
+  EX_SIMT_CASE(14, false, EX_DTYPE_F16)
+  EX_SIMT_CASE(15, true, EX_DTYPE_BF16)
+  EX_SIMT_CASE(15, true, EX_DTYPE_F32)
+  EX_SIMT_CASE(15, true, EX_DTYPE_F16)
+  EX_SIMT_CASE(15, false, EX_DTYPE_BF16)
+  EX_SIMT_CASE(15, false, EX_DTYPE_F32)
+  EX_SIMT_CASE(15, false, EX_DTYPE_F16)
+#undef EX_SIMT_CASE
+  return cudaErrorInvalidValue;
+}
+
+// Shared argument validation of ex_linear / ex_linear_partial_i64.
+int check_linear_args(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* cx, const int8_t* wh,
+                      const int8_t* wl, int64_t ldw, const int32_t* cw, int64_t M, int64_t N, int64_t K, int F,
+                      const void* out, int64_t ldo) {
+  if (M < 0 || N < 0 || K < 0 || M > INT32_MAX || N > INT32_MAX) return EX_ERR_ARG;
+  if (K > ex::EX_MAX_K) return EX_ERR_UNSUPPORTED;
+  if (F != 14 && F != 15) return EX_ERR_ARG;
+  if (M == 0 || N == 0) return EX_OK;
+  if (!out || ldo < N) return EX_ERR_ARG;
+  if (K > 0 && (!xh || !xl || !wh || !wl || ldx < K || ldw < K)) return EX_ERR_ARG;
+  if (F == 15 && (!cx || !cw)) return EX_ERR_ARG;
+  return EX_OK;
+}
+
+// Algorithm choice for EX_ALGO_AUTO: the tcgen05 int8 kernel whenever its TMA alignment rules hold, else SIMT.
+int pick_algo(int algo, const int8_t* xh, const int8_t* xl, int64_t ldx, const int8_t* wh, const int8_t* wl,
+              int64_t ldw, int64_t M, int64_t N, int64_t K) {
+  if (algo != EX_ALGO_AUTO) return algo;
+  if (ex::tc_supported(xh, xl, ldx, wh, wl, ldw, M, N, K)) return EX_ALGO_TC_I8;
+  return EX_ALGO_SIMT;
+}
+
+template <bool PARTIAL>
+int linear_impl(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* cx, const int32_t* sx,
+                const int8_t* wh, const int8_t* wl, int64_t ldw, const int32_t* cw, const int32_t* sw, int64_t M,
+                int64_t N, int64_t K, int F, int trunc, void* out, int out_dtype, int64_t ldo, void* workspace,
+                size_t workspace_bytes, int split_k, int algo, cudaStream_t st) {
+  int rc = check_linear_args(xh, xl, ldx, cx, wh, wl, ldw, cw, M, N, K, F, out, ldo);
+  if (rc != EX_OK || M == 0 || N == 0) return rc;
+  if (!PARTIAL && (!sx || !sw)) return EX_ERR_ARG;
+  if (!PARTIAL && !dtype_ok(out_dtype)) return EX_ERR_DTYPE;
+  if (split_k < 0) return EX_ERR_ARG;
+  algo = pick_algo(algo, xh, xl, ldx, wh, wl, ldw, M, N, K);
+  if (algo == EX_ALGO_SIMT) {
+    const SimtPlan p = simt_plan(M, N, K, split_k);
+    if (p.ws_bytes > 0 && (!workspace || workspace_bytes < p.ws_bytes)) return EX_ERR_WORKSPACE;
+    if (p.ws_bytes > 0 && reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return EX_ERR_ALIGN;
+    return cuda_status(launch_simt<PARTIAL>(F, trunc, out_dtype, xh, xl, ldx, cx, sx, wh, wl, ldw, cw, sw, (int)M,
+                                            (int)N, (int)K, p, out, ldo, workspace, st));
+  }
+  if (algo == EX_ALGO_TC_BF16) return EX_ERR_UNSUPPORTED;
+  if (algo == EX_ALGO_TC_I8) {
+    if (!ex::tc_supported(xh, xl, ldx, wh, wl, ldw, M, N, K)) return EX_ERR_ALIGN;
+    const ex::TcPlan p = ex::tc_plan(M, N, K, split_k, algo, num_sms());
+    if (p.ws_bytes > 0 && (!workspace || workspace_bytes < p.ws_bytes)) return EX_ERR_WORKSPACE;
+    if (p.ws_bytes > 0 && reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return EX_ERR_ALIGN;
+    cudaError_t e = ex::launch_tc<PARTIAL>(p, F, trunc, out_dtype, xh, xl, ldx, cx, sx, wh, wl, ldw, cw, sw, (int)M,
+                                           (int)N, (int)K, out, ldo, workspace, st);
+    if (e == cudaErrorNotSupported) return EX_ERR_UNSUPPORTED;
+    return cuda_status(e);
+  }
+  return EX_ERR_ARG;
+}
+
+size_t linear_ws(int64_t M, int64_t N, int64_t K, int split_k, int algo) {
+  if (M <= 0 || N <= 0) return 0;
+  if (algo == EX_ALGO_AUTO) algo = EX_ALGO_TC_I8;  // TC plans need at least as much as SIMT ones, sized generously
+  size_t a = simt_plan(M, N, K, split_k).ws_bytes;
+  size_t b = (algo == EX_ALGO_SIMT) ? 0 : ex::tc_plan(M, N, K, split_k, algo, num_sms()).ws_bytes;
+  return std::max(a, b);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ex_version(void) { return "vllm-exact-b200 0.1.0 (sm_100a)"; }
+
+const char* ex_status_string(int s) {
+  switch (s) {
+    case EX_OK: return "ok";
+    case EX_ERR_ARG: return "invalid argument";
+    case EX_ERR_ALIGN: return "misaligned pointer or leading dimension";
+    case EX_ERR_WORKSPACE: return "workspace missing or too small";
+    case EX_ERR_DTYPE: return "unsupported dtype";
+    case EX_ERR_UNSUPPORTED: return "unsupported shape or algorithm";
+    case EX_ERR_CUDA: return "CUDA error";
+    case EX_ERR_DEVICE: return "device-side bounded wait timed out";
+    default: return "unknown status";
+  }
+}
+
+const char* ex_last_error_string(void) { return g_last_error.c_str(); }
+
+int ex_device_error(int* code) {
+  if (!code) return EX_ERR_ARG;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_status(e);
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_ex_dev_error, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e);
+  const int zero = 0;
+  e = cudaMemcpyToSymbol(g_ex_dev_error, &zero, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e);
+  *code = v;
+  return EX_OK;
+}
+
+int ex_digitize(const void* x, int x_dtype, int64_t ldx, int64_t rows, int64_t K, int F, int8_t* h, int8_t* l,
+                int64_t ldd, int32_t* cs, int32_t* sh, void* stream) {
+  if (rows < 0 || K < 0 || rows > INT32_MAX || K > INT32_MAX) return EX_ERR_ARG;
+  if (F != 14 && F != 15) return EX_ERR_ARG;
+  if (!dtype_ok(x_dtype)) return EX_ERR_DTYPE;
+  if (rows == 0) return EX_OK;
+  if (!cs || !sh) return EX_ERR_ARG;
+  if (K > 0 && (!x || !h || !l || ldx < K || ldd < K)) return EX_ERR_ARG;
+  return cuda_status(
+      ex::launch_digitize<ex::DIG_LOCAL>(x, x_dtype, ldx, rows, K, F, h, l, ldd, cs, sh, nullptr, (cudaStream_t)stream));
+}
+
+int ex_row_absmax(const void* x, int x_dtype, int64_t ldx, int64_t rows, int64_t K, float* amax, void* stream) {
+  if (rows < 0 || K < 0 || rows > INT32_MAX || K > INT32_MAX) return EX_ERR_ARG;
+  if (!dtype_ok(x_dtype)) return EX_ERR_DTYPE;
+  if (rows == 0) return EX_OK;
+  if (!amax || (K > 0 && (!x || ldx < K))) return EX_ERR_ARG;
+  return cuda_status(ex::launch_digitize<ex::DIG_ABSMAX>(x, x_dtype, ldx, rows, K, 14, nullptr, nullptr, K, nullptr,
+                                                         nullptr, amax, (cudaStream_t)stream));
+}
+
+int ex_digitize_given_absmax(const void* x, int x_dtype, int64_t ldx, int64_t rows, int64_t K, int F,
+                             const float* amax, int8_t* h, int8_t* l, int64_t ldd, int32_t* cs, int32_t* sh,
+                             void* stream) {
+  if (rows < 0 || K < 0 || rows > INT32_MAX || K > INT32_MAX) return EX_ERR_ARG;
+  if (F != 14 && F != 15) return EX_ERR_ARG;
+  if (!dtype_ok(x_dtype)) return EX_ERR_DTYPE;
+  if (rows == 0) return EX_OK;
+  if (!cs || !sh || !amax) return EX_ERR_ARG;
+  if (K > 0 && (!x || !h || !l || ldx < K || ldd < K)) return EX_ERR_ARG;
+  return cuda_status(ex::launch_digitize<ex::DIG_GIVEN>(x, x_dtype, ldx, rows, K, F, h, l, ldd, cs, sh,
+                                                        const_cast<float*>(amax), (cudaStream_t)stream));
+}
+
+size_t ex_linear_workspace_bytes(int64_t M, int64_t N, int64_t K, int split_k, int algo) {
+  return linear_ws(M, N, K, split_k, algo);
+}
+
+int ex_linear(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* cx, const int32_t* sx,
+              const int8_t* wh, const int8_t* wl, int64_t ldw, const int32_t* cw, const int32_t* sw, int64_t M,
+              int64_t N, int64_t K, int F, int trunc, void* out, int out_dtype, int64_t ldo, void* workspace,
+              size_t workspace_bytes, int split_k, int algo, void* stream) {
+  return linear_impl<false>(xh, xl, ldx, cx, sx, wh, wl, ldw, cw, sw, M, N, K, F, trunc, out, out_dtype, ldo,
+                            workspace, workspace_bytes, split_k, algo, (cudaStream_t)stream);
+}
+
+int ex_linear_partial_i64(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* cx, const int8_t* wh,
+                          const int8_t* wl, int64_t ldw, const int32_t* cw, int64_t M, int64_t N, int64_t K, int F,
+                          int trunc, int64_t* tot, int64_t ldt, void* workspace, size_t workspace_bytes, int split_k,
+                          int algo, void* stream) {
+  return linear_impl<true>(xh, xl, ldx, cx, nullptr, wh, wl, ldw, cw, nullptr, M, N, K, F, trunc, tot,
+                           EX_DTYPE_F32, ldt, workspace, workspace_bytes, split_k, algo, (cudaStream_t)stream);
+}
+
+int ex_epilogue_i64(const int64_t* tot, int64_t ldt, const int32_t* sx, const int32_t* sw, int64_t M, int64_t N,
+                    void* out, int out_dtype, int64_t ldo, void* stream) {
+  if (M < 0 || N < 0 || M > INT32_MAX || N > INT32_MAX) return EX_ERR_ARG;
+  if (!dtype_ok(out_dtype)) return EX_ERR_DTYPE;
+  if (M == 0 || N == 0) return EX_OK;
+  if (!tot || !sx || !sw || !out || ldt < N || ldo < N) return EX_ERR_ARG;
+  const int64_t total = M * N;
+  const int threads = 256;
+  const int blocks = (int)std::min<int64_t>(cdiv(total, threads), 16 * (int64_t)num_sms());
+  cudaStream_t st = (cudaStream_t)stream;
+  const long long* t = reinterpret_cast<const long long*>(tot);
+  if (out_dtype == EX_DTYPE_F32)
+    ex::k_epilogue_i64<EX_DTYPE_F32><<<blocks, threads, 0, st>>>(t, ldt, sx, sw, (int)M, (int)N, out, ldo);
+  else if (out_dtype == EX_DTYPE_BF16)
+    ex::k_epilogue_i64<EX_DTYPE_BF16><<<blocks, threads, 0, st>>>(t, ldt, sx, sw, (int)M, (int)N, out, ldo);
+  else
+    ex::k_epilogue_i64<EX_DTYPE_F16><<<blocks, threads, 0, st>>>(t, ldt, sx, sw, (int)M, (int)N, out, ldo);
+  return cuda_status(cudaGetLastError());
+}
+
+size_t ex_paged_decode_workspace_bytes(int n, int H, int D, int max_len, int split) {
+  if (n <= 0 || H <= 0 || D <= 0 || split <= 0) return 0;
+  const int64_t NS = std::max<int64_t>(1, cdiv(max_len, split));
+  const int64_t rows = (int64_t)n * H * NS;
+  return align_up((size_t)rows * 4, 256) * 2 + (size_t)rows * D * 4;
+}
+
+int ex_paged_decode(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cache, const void* v_cache,
+                    int64_t s_block, int64_t s_page, int64_t s_head, const int32_t* block_table, int64_t sbt,
+                    const int32_t* seq_lens, int n, int H, int KV, int D, int BS, float scale, int max_len, int split,
+                    void* out, int64_t so_t, int64_t so_h, int out_dtype, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  if (n < 0 || H <= 0 || KV <= 0 || H % KV != 0 || BS <= 0 || split <= 0 || max_len < 0) return EX_ERR_ARG;
+  const int G = H / KV;
+  if (G > 16) return EX_ERR_UNSUPPORTED;
+  if (D != 64 && D != 128 && D != 256) return EX_ERR_UNSUPPORTED;
+  if (!dtype_ok(out_dtype)) return EX_ERR_DTYPE;
+  if (n == 0) return EX_OK;
+  if (!q || !k_cache || !v_cache || !block_table || !seq_lens || !out) return EX_ERR_ARG;
+  // 16-byte cp.async gathers and 4-byte query loads
+  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) % 16 != 0 ||
+      s_block % 8 != 0 || s_page % 8 != 0 || s_head % 8 != 0)
+    return EX_ERR_ALIGN;
+  if (reinterpret_cast<uintptr_t>(q) % 4 != 0 || sq_t % 2 != 0 || sq_h % 2 != 0) return EX_ERR_ALIGN;
+  const size_t need = ex_paged_decode_workspace_bytes(n, H, D, max_len, split);
+  if (!workspace || workspace_bytes < need) return EX_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return EX_ERR_ALIGN;
+  const int NS = (int)std::max<int64_t>(1, cdiv(max_len, split));
+  if (KV > 65535 || NS > 65535) return EX_ERR_UNSUPPORTED;
+  const int64_t rows = (int64_t)n * H * NS;
+  float* ws_m = reinterpret_cast<float*>(workspace);
+  float* ws_l = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + align_up((size_t)rows * 4, 256));
+  float* ws_acc = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + 2 * align_up((size_t)rows * 4, 256));
+  cudaStream_t st = (cudaStream_t)stream;
+  const __nv_bfloat16* qp = reinterpret_cast<const __nv_bfloat16*>(q);
+  const __nv_bfloat16* kp = reinterpret_cast<const __nv_bfloat16*>(k_cache);
+  const __nv_bfloat16* vp = reinterpret_cast<const __nv_bfloat16*>(v_cache);
+  dim3 grid(n, KV, NS);
+  cudaError_t e = cudaSuccess;
+#define EX_PD_LAUNCH(DD)                                                                                         \
+  {                                                                                                              \
+    const int smem = ex::PdCfg<DD>::SMEM;                                                                        \
+    e = cudaFuncSetAttribute(ex::k_paged_partial<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);        \
+    if (e == cudaSuccess)                                                                                        \
+      ex::k_paged_partial<DD><<<grid, ex::PD_THREADS, smem, st>>>(qp, sq_t, sq_h, kp, vp, s_block, s_page,       \
+                                                                   s_head, block_table, sbt, seq_lens, H, G, BS, \
+                                                                   scale, split, NS, ws_m, ws_l, ws_acc);        \
+  }
+  if (D == 64) EX_PD_LAUNCH(64)
+  else if (D == 128) EX_PD_LAUNCH(128)
+  else EX_PD_LAUNCH(256)
+#undef EX_PD_LAUNCH
+  if (e != cudaSuccess) return cuda_status(e);
+  if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e);
+  const int mthreads = std::min(D, 256);
+  if (out_dtype == EX_DTYPE_BF16)
+    ex::k_paged_merge<EX_DTYPE_BF16><<<n * H, mthreads, 0, st>>>(ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
+  else if (out_dtype == EX_DTYPE_F16)
+    ex::k_paged_merge<EX_DTYPE_F16><<<n * H, mthreads, 0, st>>>(ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
+  else
+    ex::k_paged_merge<EX_DTYPE_F32><<<n * H, mthreads, 0, st>>>(ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
+  return cuda_status(cudaGetLastError());
+}
+
+}  // extern "C"

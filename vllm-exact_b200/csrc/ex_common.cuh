@@ -1,0 +1,256 @@
+// Common device helpers for the vllm-exact B200 library: status codes, the device error word, numeric helpers of
+// the exact epilogue, and thin inline-PTX wrappers for mbarriers, TMA and tcgen05 (sm_100a).
+//
+// Every spin-wait in this library is bounded: after EX_WAIT_TIMEOUT_NS of global time the waiting thread records
+// an error in g_ex_dev_error and gives up, so a broken pipeline ends with an error status instead of a hung GPU.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "vllm_exact_b200.h"
+
+#define EX_WAIT_TIMEOUT_NS 2000000000ull  // 2 s: far above any legitimate in-kernel wait
+
+// Device error word. 0 = fine; otherwise the code of the first failure (EX_DEVERR_*). Read and cleared by the host
+// through ex_device_error().
+__device__ int g_ex_dev_error;
+
+enum {
+  EX_DEVERR_NONE = 0,
+  EX_DEVERR_WAIT_TMA = 1,      // a consumer gave up waiting for a TMA load
+  EX_DEVERR_WAIT_SLOT = 2,     // the producer gave up waiting for a free pipeline slot
+  EX_DEVERR_WAIT_MMA = 3,      // the epilogue gave up waiting for the accumulator
+  EX_DEVERR_WAIT_TMEM = 4,     // the MMA warp gave up waiting for the epilogue to release TMEM
+  EX_DEVERR_TMEM_ALLOC = 5,    // TMEM allocation returned an unexpected address
+};
+
+__device__ __forceinline__ void ex_set_error(int code) { atomicCAS(&g_ex_dev_error, 0, code); }
+
+__device__ __forceinline__ uint64_t ex_globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// Exact epilogue numerics (reference kernels.py:98-100 and :154-157):
+//   y = float32( float64(tot) * 2^-(sx+sw) ), the power of two built from float64 bits with int64 arithmetic.
+// int64 -> float64 is exact (|tot| < 2^53), the product by a power of two is exact, float64 -> float32 rounds once
+// to nearest even. A bf16/fp16 output then rounds once more from that float32 (the reference's double rounding).
+// ------------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ float ex_scale_to_f32(long long tot, int sx, int sw) {
+  long long e = -((long long)sx + (long long)sw);
+  unsigned long long bits = ((unsigned long long)(e + 1023)) << 52;
+  double scale = __longlong_as_double((long long)bits);
+  return __double2float_rn(__dmul_rn(__ll2double_rn(tot), scale));
+}
+
+template <int OUT_DTYPE>
+__device__ __forceinline__ void ex_store_out(void* out, long long idx, float v) {
+  if constexpr (OUT_DTYPE == EX_DTYPE_F32) {
+    reinterpret_cast<float*>(out)[idx] = v;
+  } else if constexpr (OUT_DTYPE == EX_DTYPE_BF16) {
+    reinterpret_cast<__nv_bfloat16*>(out)[idx] = __float2bfloat16_rn(v);
+  } else {
+    reinterpret_cast<__half*>(out)[idx] = __float2half_rn(v);
+  }
+}
+
+// Integer total of the two-digit product plus the F=15 offset correction (reference kernels.py:93-97, :143, :148-151).
+__device__ __forceinline__ long long ex_combine(int hh, int md, int ll) {
+  return ((long long)hh << 16) + ((long long)md << 8) + (long long)ll;
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// shared-memory address helpers
+// ------------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t ex_smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// mbarrier
+// ------------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(ex_smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(ex_smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                   ex_smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(ex_smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase. Returns false (and records `code`) if the phase did not complete within
+// EX_WAIT_TIMEOUT_NS. Once any thread has recorded an error the others give up quickly too.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = ex_globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0) {
+      const uint64_t dt = ex_globaltimer() - t0;
+      if (dt > EX_WAIT_TIMEOUT_NS) {
+        ex_set_error(code);
+        return false;
+      }
+      if (dt > 1000000ull && *(volatile int*)&g_ex_dev_error != 0) return false;  // someone else already failed
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// TMA (cp.async.bulk.tensor), tiled 2D loads into this CTA's shared memory, completion counted on an mbarrier.
+// Loads only: no store/reduce forms, and no cluster-wide forms are used anywhere in this library.
+// ------------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, %4}], "
+      "[%2], %5;" ::"r"(ex_smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(ex_smem_u32(bar)), "r"(c0), "r"(c1), "l"(cache_hint)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// L2 cache-policy hints (createpolicy): weights are streamed once, activations are re-read by every CTA.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// tcgen05 (5th-generation tensor cores, tensor memory)
+// ------------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(ex_smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Arrive on `bar` once all tcgen05.mma previously issued by this thread have completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(ex_smem_u32(bar))
+               : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, int8 x int8 -> int32, both operands K-major.
+__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, bf16 x bf16 -> fp32, both operands K-major.
+__device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 32 bit, 16 consecutive columns per thread (thread i of the warp reads TMEM lane base+i).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for a K-major operand tile in the 128-byte swizzled layout written by TMA
+// (CU_TENSOR_MAP_SWIZZLE_128B): rows of 128 bytes, 8-row atoms of 1024 bytes. Fields (sm_100 UMMA descriptor):
+// start address >> 4 in bits [0,14), leading byte offset >> 4 in [16,30) (unused for swizzled K-major; 16 bytes),
+// stride byte offset >> 4 in [32,46) (1024 bytes between 8-row atoms), version 1 in [46,48), base offset 0,
+// layout type 2 (128-byte swizzle) in [61,64). The tile must start on a 1024-byte boundary; stepping along K inside
+// the 128-byte row is done by adding the byte offset to the start address.
+__device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+  d |= (uint64_t)(16 >> 4) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor of tcgen05.mma (sm_100): D format in bits [4,6) (1 = f32, 2 = s32), A format [7,10),
+// B format [10,13) (kind::f16: 1 = bf16; kind::i8: 1 = signed), A/B K-major (bits 15,16 = 0), N >> 3 in [17,23),
+// M >> 4 in [24,29).
+__host__ __device__ constexpr uint32_t make_idesc_i8(int M, int N) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+__host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b32 r;\n\t"
+      "elect.sync r|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred;
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// int64 reduction into the split-K workspace: relaxed atomic add at L2. Integer addition is associative and
+// commutative, so the final value does not depend on the order in which CTAs arrive.
+// ------------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void red_add_s64(long long* p, long long v) {
+  asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}

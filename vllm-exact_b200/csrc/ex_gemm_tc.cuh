@@ -1,0 +1,496 @@
+// Exact two-digit GEMM on 5th-generation tensor cores (EX_ALGO_TC_I8), sm_100a.
+//
+// Same integers as the reference's _exact_kernel / _exact_bf16_kernel (kernels.py:103-157, :180-247), computed with
+// tcgen05.mma kind::i8 (int8 x int8 -> int32, exact) from TMA-loaded digit tiles, int32 accumulators in tensor
+// memory, int64 combine and the exact epilogue fused in.
+//
+// Orientation ("swap-AB"): the MMA's M dimension is 128 weight rows, its N dimension is the token tile (BT tokens),
+// so decode batches (M <= 64) still fill the 128-row tensor-core datapath. Per K step of 128 bytes the CTA holds
+//   Wh, Wl : 128 x 128 int8 (16 KB each)          A operands
+//   X      : [xh rows 0..BT) ; [xl rows BT..2BT)   B operand (xh and xl stacked along N)
+// and issues
+//   MMA1  D[hh | md] (+)= Wh . [Xh ; Xl]^T     (N = 2 BT)  -> hh = Wh.Xh, md = Wh.Xl
+//   MMA2  D[md]      +=  Wl . Xh^T             (N = BT)    -> md += Wl.Xh
+//   MMA3  D[ll]      (+)= Wl . Xl^T            (N = BT, only without truncation)
+// so md holds xh.wl + xl.wh directly. int32 is exact: |md| <= 2^15 K < 2^31 for K <= 65536.
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer, warps 2..5 = epilogue
+// (TMEM -> registers -> int64 combine -> scale -> store). Two TMEM accumulator buffers let the epilogue of one
+// segment overlap the MMAs of the next.
+//
+// Work partition: the (tile, k-iteration) space is flattened (tiles ordered n-major, m-minor so the m-tiles that
+// share a weight tile run back to back) and cut into G equal contiguous ranges, one per CTA. A CTA's range is a list
+// of segments (tile, k_begin, k_end). A segment covering a whole tile is written directly; otherwise its int64
+// totals are added into a workspace with relaxed atomics and a per-tile ticket counting k-iterations elects the CTA
+// that completes the tile, which applies the epilogue and zeroes the workspace again. Integer addition is exact and
+// order-free, so the result bits do not depend on G, on the split, or on arrival order.
+#pragma once
+#include "ex_common.cuh"
+
+namespace ex {
+
+constexpr int64_t EX_MAX_K = 65536;  // int32 accumulators: |md| <= 2^15 K must stay below 2^31
+constexpr int TC_THREADS = 192;
+constexpr int TC_BK = 128;               // K bytes (int8 elements) per pipeline stage = one 128-byte swizzle row
+constexpr int TC_WTILE = 128 * TC_BK;    // bytes of one weight digit tile
+constexpr int TC_SMEM_BUDGET = 220 * 1024;
+constexpr int TC_TMEM_COLS = 512;
+
+struct TcPlan {
+  int BT;        // token tile
+  int m_tiles, n_tiles, KI;
+  int64_t T;     // total k-iterations = tiles * KI
+  int G;         // CTAs
+  int stages;
+  size_t smem;
+  size_t ws_bytes;
+  size_t cnt_bytes;
+};
+
+struct TcArgs {
+  const int32_t* cx;
+  const int32_t* sx;
+  const int32_t* cw;
+  const int32_t* sw;
+  void* out;
+  int64_t ldo;
+  long long* ws_acc;
+  int* ws_cnt;
+  int M, N, K;
+  int F, trunc, out_dtype, partial;
+  int m_tiles, KI;
+  int64_t T;
+  int G;
+  int stages;
+};
+
+struct TcSeg {
+  int tile, kb, ke;
+};
+
+// Segment walker shared by all roles: CTA c owns k-iterations [c*T/G, (c+1)*T/G).
+struct TcWalk {
+  int64_t it, it1;
+  int KI;
+  __device__ TcWalk(const TcArgs& a) {
+    it = (a.T * (int64_t)blockIdx.x) / a.G;
+    it1 = (a.T * (int64_t)(blockIdx.x + 1)) / a.G;
+    KI = a.KI;
+  }
+  __device__ bool next(TcSeg& s) {
+    if (it >= it1) return false;
+    s.tile = (int)(it / KI);
+    s.kb = (int)(it % KI);
+    s.ke = (int)min((int64_t)KI, (int64_t)s.kb + (it1 - it));
+    it += s.ke - s.kb;
+    return true;
+  }
+};
+
+__device__ __forceinline__ void tc_finish(long long tot, int t, int n, const TcArgs& a) {
+  if (a.F == 15) tot += 128ll * ((long long)a.cx[t] + (long long)a.cw[n]) + 16384ll * (long long)a.K;
+  const int64_t idx = (int64_t)t * a.ldo + n;
+  if (a.partial) {
+    reinterpret_cast<long long*>(a.out)[idx] = tot;
+    return;
+  }
+  const float y = ex_scale_to_f32(tot, a.sx[t], a.sw[n]);
+  if (a.out_dtype == EX_DTYPE_BF16)
+    reinterpret_cast<__nv_bfloat16*>(a.out)[idx] = __float2bfloat16_rn(y);
+  else if (a.out_dtype == EX_DTYPE_F32)
+    reinterpret_cast<float*>(a.out)[idx] = y;
+  else
+    reinterpret_cast<__half*>(a.out)[idx] = __float2half_rn(y);
+}
+
+template <int CW>
+__device__ __forceinline__ void tmem_ldc(uint32_t taddr, uint32_t (&r)[CW]) {
+  if constexpr (CW == 16)
+    tmem_ld16(taddr, r);
+  else
+    tmem_ld8(taddr, r);
+}
+
+template <int BT>
+struct TcLayout {
+  static constexpr int XTILE = 2 * BT * TC_BK;  // bytes of the stacked activation tile
+  static constexpr int STAGE = 2 * TC_WTILE + XTILE;
+  static constexpr int CB_TRUNC = 2 * BT;       // TMEM columns per accumulator buffer
+  static constexpr int CB_FULL = 3 * BT;
+  static_assert(BT % 8 == 0 && BT >= 8 && BT <= 128, "token tile");
+};
+
+template <int BT>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    k_exact_tc_i8(const __grid_constant__ CUtensorMap tm_wh, const __grid_constant__ CUtensorMap tm_wl,
+                  const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl,
+                  const TcArgs a) {
+  using Lay = TcLayout<BT>;
+  extern __shared__ uint8_t tc_smem_raw[];
+  // 1024-byte alignment for the 128-byte-swizzled tiles
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = a.stages;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + (size_t)S * Lay::STAGE);
+  uint64_t* empty_bar = full_bar + S;
+  uint64_t* tfull_bar = empty_bar + S;   // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;  // [2]
+  uint64_t* done_bar = tempty_bar + 2;   // MMA completion before teardown
+  uint64_t* epi_bar = done_bar + 1;      // epilogue threads finished their atomic adds
+  uint64_t* flag_bar = epi_bar + 1;      // ticket result published
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(flag_bar + 1);
+  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cb = a.trunc ? Lay::CB_TRUNC : Lay::CB_FULL;
+  const int nbuf = (2 * cb <= TC_TMEM_COLS) ? 2 : 1;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(full_bar + i, 1);
+      mbar_init(empty_bar + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(tfull_bar + i, 1);
+      mbar_init(tempty_bar + i, 128);
+    }
+    mbar_init(done_bar, 1);
+    mbar_init(epi_bar, 128);
+    mbar_init(flag_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_wh);
+    tma_prefetch_desc(&tm_wl);
+    tma_prefetch_desc(&tm_xh);
+    tma_prefetch_desc(&tm_xl);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TC_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      TcWalk walk(a);
+      TcSeg sg;
+      int stage = 0;
+      uint32_t phase = 0;
+      int64_t issued = 0;
+      bool ok = true;
+      while (ok && walk.next(sg)) {
+        const int n_tile = sg.tile / a.m_tiles, m_tile = sg.tile % a.m_tiles;
+        for (int kt = sg.kb; kt < sg.ke; ++kt) {
+          if (!mbar_wait(empty_bar + stage, phase ^ 1, EX_DEVERR_WAIT_SLOT)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + (size_t)stage * Lay::STAGE;
+          mbar_arrive_expect_tx(full_bar + stage, Lay::STAGE);
+          const int kc = kt * TC_BK;
+          tma_load_2d(st, &tm_wh, full_bar + stage, kc, n_tile * 128, pol_w);
+          tma_load_2d(st + TC_WTILE, &tm_wl, full_bar + stage, kc, n_tile * 128, pol_w);
+          tma_load_2d(st + 2 * TC_WTILE, &tm_xh, full_bar + stage, kc, m_tile * BT, pol_x);
+          tma_load_2d(st + 2 * TC_WTILE + BT * TC_BK, &tm_xl, full_bar + stage, kc, m_tile * BT, pol_x);
+          ++issued;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // wait for every load still in flight before the CTA may exit (bounded)
+      const int64_t pending = issued < S ? issued : S;
+      for (int64_t i = 0; i < pending; ++i) {
+        if (--stage < 0) {
+          stage = S - 1;
+          phase ^= 1;
+        }
+        mbar_wait(full_bar + stage, phase, EX_DEVERR_WAIT_TMA);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_2bt = make_idesc_i8(128, 2 * BT);
+      const uint32_t idesc_bt = make_idesc_i8(128, BT);
+      TcWalk walk(a);
+      TcSeg sg;
+      int stage = 0;
+      uint32_t phase = 0;
+      int seg_i = 0;
+      bool ok = true;
+      while (ok && walk.next(sg)) {
+        const int buf = nbuf == 2 ? (seg_i & 1) : 0;
+        const uint32_t use = nbuf == 2 ? (uint32_t)(seg_i >> 1) : (uint32_t)seg_i;  // uses of this buffer so far
+        if (!mbar_wait(tempty_bar + buf, (use & 1) ^ 1, EX_DEVERR_WAIT_TMEM)) break;
+        tc_fence_after();
+        const uint32_t d_hh = tmem_base + (uint32_t)(buf * cb);
+        const uint32_t d_md = d_hh + BT;
+        const uint32_t d_ll = d_hh + 2 * BT;
+        for (int kt = sg.kb; kt < sg.ke; ++kt) {
+          if (!mbar_wait(full_bar + stage, phase, EX_DEVERR_WAIT_TMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = ex_smem_u32(smem + (size_t)stage * Lay::STAGE);
+          const uint64_t dwh = make_sw128_desc(st);
+          const uint64_t dwl = make_sw128_desc(st + TC_WTILE);
+          const uint64_t dxh = make_sw128_desc(st + 2 * TC_WTILE);
+          const uint64_t dxl = make_sw128_desc(st + 2 * TC_WTILE + BT * TC_BK);
+#pragma unroll
+          for (int j = 0; j < TC_BK / 32; ++j) {  // 32-byte K steps inside the swizzled row (+2 in 16-byte units)
+            const uint64_t o = (uint64_t)(2 * j);
+            const uint32_t acc = (kt > sg.kb || j > 0) ? 1u : 0u;
+            tc_mma_i8(d_hh, dwh + o, dxh + o, idesc_2bt, acc);
+            tc_mma_i8(d_md, dwl + o, dxh + o, idesc_bt, 1u);
+            if (!a.trunc) tc_mma_i8(d_ll, dwl + o, dxl + o, idesc_bt, acc);
+          }
+          tc_commit(empty_bar + stage);  // frees this smem stage once the MMAs above have read it
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(tfull_bar + buf);  // accumulator of this segment is complete
+        ++seg_i;
+      }
+      tc_commit(done_bar);
+      mbar_wait(done_bar, 0, EX_DEVERR_WAIT_MMA);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;            // TMEM lane quarter this warp may access
+    const int row = 32 * q + lane;     // weight row inside the tile = TMEM lane
+    const int et = threadIdx.x - 64;   // 0..127
+    const uint32_t lane_off = (uint32_t)(32 * q) << 16;
+    TcWalk walk(a);
+    TcSeg sg;
+    int seg_i = 0;
+    uint32_t epi_phase = 0;
+    while (walk.next(sg)) {
+      const int buf = nbuf == 2 ? (seg_i & 1) : 0;
+      const uint32_t use = nbuf == 2 ? (uint32_t)(seg_i >> 1) : (uint32_t)seg_i;
+      if (!mbar_wait(tfull_bar + buf, use & 1, EX_DEVERR_WAIT_MMA)) break;
+      tc_fence_after();
+      const int n_tile = sg.tile / a.m_tiles, m_tile = sg.tile % a.m_tiles;
+      const int n = n_tile * 128 + row;
+      const int m0 = m_tile * BT;
+      const bool whole = (sg.kb == 0 && sg.ke == a.KI);
+      const uint32_t t_hh = tmem_base + lane_off + (uint32_t)(buf * cb);
+constexpr int CW = BT < 16 ? 8 : 16;  // TMEM columns read per tcgen05.ld
+#pragma unroll 1
+      for (int c = 0; c < BT; c += CW) {
+        uint32_t vh[CW], vm[CW], vl[CW];
+        tmem_ldc<CW>(t_hh + c, vh);
+        tmem_ldc<CW>(t_hh + BT + c, vm);
+        if (!a.trunc) tmem_ldc<CW>(t_hh + 2 * BT + c, vl);
+        tmem_ld_wait();
+        if (c + CW >= BT) {  // every TMEM read of this buffer is done: hand it back to the MMA warp
+          tc_fence_before();
+          mbar_arrive(tempty_bar + buf);
+        }
+        if (n < a.N) {
+#pragma unroll
+          for (int j = 0; j < CW; ++j) {
+            const int t = m0 + c + j;
+            if (t < a.M) {
+              const long long tot = ex_combine((int)vh[j], (int)vm[j], a.trunc ? 0 : (int)vl[j]);
+              if (whole)
+                tc_finish(tot, t, n, a);
+              else
+                red_add_s64(a.ws_acc + (int64_t)t * a.N + n, tot);
+            }
+          }
+        }
+      }
+      ++seg_i;
+      if (whole) continue;
+      // split tile: ticket on k-iterations; the CTA that completes the tile finishes it
+      __threadfence();
+      mbar_arrive(epi_bar);
+      if (et == 0) {
+        int flag = 0;
+        if (mbar_wait(epi_bar, epi_phase, EX_DEVERR_WAIT_MMA)) {
+          const int old = atomicAdd(a.ws_cnt + sg.tile, sg.ke - sg.kb);
+          flag = (old + (sg.ke - sg.kb) == a.KI) ? 1 : 0;
+          if (flag) a.ws_cnt[sg.tile] = 0;
+        }
+        *(volatile int*)last_flag = flag;
+        mbar_arrive(flag_bar);
+      }
+      if (!mbar_wait(flag_bar, epi_phase, EX_DEVERR_WAIT_MMA)) break;
+      epi_phase ^= 1;
+      if (*(volatile int*)last_flag) {
+        __threadfence();
+        if (n < a.N) {
+          const int tmax = min(BT, a.M - m0);
+          for (int j = 0; j < tmax; ++j) {
+            const int t = m0 + j;
+            const long long tot = (long long)atomicExch(
+                reinterpret_cast<unsigned long long*>(a.ws_acc + (int64_t)t * a.N + n), 0ull);
+            tc_finish(tot, t, n, a);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TC_TMEM_COLS);
+  }
+}
+
+// --------------------------------------------------------------------------------------------------------------
+// host side
+// --------------------------------------------------------------------------------------------------------------
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  }
+  return fn;
+}
+
+static bool device_is_sm100() {
+  static int cached = -1;
+  if (cached < 0) {
+    int dev = 0, major = 0, minor = 0;
+    cached = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) == cudaSuccess)
+      cached = (major == 10 && minor == 0) ? 1 : 0;
+  }
+  return cached == 1;
+}
+
+// TMA rules: 16-byte aligned bases and leading dimensions (bytes); K within the int32-exact range.
+static bool tc_supported(const int8_t* xh, const int8_t* xl, int64_t ldx, const int8_t* wh, const int8_t* wl,
+                         int64_t ldw, int64_t M, int64_t N, int64_t K) {
+  if (K <= 0 || K > EX_MAX_K || M <= 0 || N <= 0) return false;
+  if (ldx % 16 != 0 || ldw % 16 != 0) return false;
+  const uintptr_t o = reinterpret_cast<uintptr_t>(xh) | reinterpret_cast<uintptr_t>(xl) |
+                      reinterpret_cast<uintptr_t>(wh) | reinterpret_cast<uintptr_t>(wl);
+  if (o % 16 != 0) return false;
+  return device_is_sm100();
+}
+
+static int tc_pick_bt(int64_t M) {
+  if (M <= 8) return 8;
+  if (M <= 16) return 16;
+  if (M <= 32) return 32;
+  if (M <= 64) return 64;
+  return 128;
+}
+
+static size_t tc_stage_bytes(int BT) { return 2 * (size_t)TC_WTILE + 2 * (size_t)BT * TC_BK; }
+
+static TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int split_k, int algo, int sms) {
+  (void)algo;
+  TcPlan p;
+  p.BT = tc_pick_bt(M);
+  p.m_tiles = (int)((M + p.BT - 1) / p.BT);
+  p.n_tiles = (int)((N + 127) / 128);
+  p.KI = (int)((K + TC_BK - 1) / TC_BK);
+  const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles;
+  p.T = tiles * p.KI;
+  int64_t G = split_k > 0 ? tiles * split_k : (int64_t)sms;
+  G = std::max<int64_t>(1, std::min<int64_t>(G, p.T));
+  G = std::min<int64_t>(G, 2147483647);
+  p.G = (int)G;
+  const size_t stage = tc_stage_bytes(p.BT);
+  const size_t overhead = 1024 + 256;  // alignment slack + barriers
+  p.stages = (int)std::min<size_t>(8, (TC_SMEM_BUDGET - overhead) / stage);
+  p.smem = (size_t)p.stages * stage + overhead;
+  const bool aligned = (G <= tiles) && (tiles % G == 0);
+  p.cnt_bytes = (size_t)((tiles * 4 + 255) / 256 * 256);
+  p.ws_bytes = aligned ? 0 : p.cnt_bytes + (size_t)M * N * 8;
+  return p;
+}
+
+static bool encode_2d_i8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_bytes,
+                         uint32_t box_inner, uint32_t box_outer) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BT>
+static cudaError_t launch_tc_bt(const TcPlan& p, const TcArgs& a, const CUtensorMap& mwh, const CUtensorMap& mwl,
+                                const CUtensorMap& mxh, const CUtensorMap& mxl, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(k_exact_tc_i8<BT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+  if (e != cudaSuccess) return e;
+  k_exact_tc_i8<BT><<<p.G, TC_THREADS, p.smem, st>>>(mwh, mwl, mxh, mxl, a);
+  return cudaGetLastError();
+}
+
+template <bool PARTIAL>
+static cudaError_t launch_tc(const TcPlan& p, int F, int trunc, int out_dtype, const int8_t* xh, const int8_t* xl,
+                             int64_t ldx, const int32_t* cx, const int32_t* sx, const int8_t* wh, const int8_t* wl,
+                             int64_t ldw, const int32_t* cw, const int32_t* sw, int M, int N, int K, void* out,
+                             int64_t ldo, void* ws, cudaStream_t st) {
+  CUtensorMap mwh, mwl, mxh, mxl;
+  if (!encode_2d_i8(&mwh, wh, K, N, ldw, TC_BK, 128) || !encode_2d_i8(&mwl, wl, K, N, ldw, TC_BK, 128) ||
+      !encode_2d_i8(&mxh, xh, K, M, ldx, TC_BK, p.BT) || !encode_2d_i8(&mxl, xl, K, M, ldx, TC_BK, p.BT))
+    return cudaErrorNotSupported;
+  TcArgs a;
+  a.cx = cx;
+  a.sx = sx;
+  a.cw = cw;
+  a.sw = sw;
+  a.out = out;
+  a.ldo = ldo;
+  a.ws_cnt = p.ws_bytes ? reinterpret_cast<int*>(ws) : nullptr;
+  a.ws_acc = p.ws_bytes ? reinterpret_cast<long long*>(reinterpret_cast<char*>(ws) + p.cnt_bytes) : nullptr;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.F = F;
+  a.trunc = trunc ? 1 : 0;
+  a.out_dtype = out_dtype;
+  a.partial = PARTIAL ? 1 : 0;
+  a.m_tiles = p.m_tiles;
+  a.KI = p.KI;
+  a.T = p.T;
+  a.G = p.G;
+  a.stages = p.stages;
+  switch (p.BT) {
+    case 8: return launch_tc_bt<8>(p, a, mwh, mwl, mxh, mxl, st);
+    case 16: return launch_tc_bt<16>(p, a, mwh, mwl, mxh, mxl, st);
+    case 32: return launch_tc_bt<32>(p, a, mwh, mwl, mxh, mxl, st);
+    case 64: return launch_tc_bt<64>(p, a, mwh, mwl, mxh, mxl, st);
+    default: return launch_tc_bt<128>(p, a, mwh, mwl, mxh, mxl, st);
+  }
+}
+
+}  // namespace ex

@@ -1,0 +1,80 @@
+"""ctypes binding of the sm_100a C ABI (include/vllm_exact_b200.h).
+
+The library is built in-tree (vllm-exact_b200/build.py) next to this file. There is no fallback: if the library is
+missing or cannot be loaded, every entry point raises.
+"""
+import ctypes
+import os
+from pathlib import Path
+
+LIB_PATH = Path(os.environ.get("VLLM_EXACT_B200_LIB", Path(__file__).with_name("libvllm_exact_b200.so")))
+
+EX_OK, EX_ERR_ARG, EX_ERR_ALIGN, EX_ERR_WORKSPACE, EX_ERR_DTYPE, EX_ERR_UNSUPPORTED, EX_ERR_CUDA, EX_ERR_DEVICE = range(8)
+EX_DTYPE_F32, EX_DTYPE_BF16, EX_DTYPE_F16 = 0, 1, 2
+EX_ALGO_AUTO, EX_ALGO_SIMT, EX_ALGO_TC_I8, EX_ALGO_TC_BF16 = 0, 1, 2, 3
+
+c_i64, c_i32, c_vp, c_sz, c_f32 = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_float
+
+# name -> (restype, argtypes); every symbol the header declares
+SIGNATURES = {
+    "ex_version": (ctypes.c_char_p, []),
+    "ex_status_string": (ctypes.c_char_p, [c_i32]),
+    "ex_last_error_string": (ctypes.c_char_p, []),
+    "ex_device_error": (c_i32, [ctypes.POINTER(c_i32)]),
+    "ex_digitize": (c_i32, [c_vp, c_i32, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp]),
+    "ex_row_absmax": (c_i32, [c_vp, c_i32, c_i64, c_i64, c_i64, c_vp, c_vp]),
+    "ex_digitize_given_absmax": (c_i32, [c_vp, c_i32, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp,
+                                         c_vp]),
+    "ex_linear_workspace_bytes": (c_sz, [c_i64, c_i64, c_i64, c_i32, c_i32]),
+    "ex_linear": (c_i32, [c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i32,
+                          c_i32, c_vp, c_i32, c_i64, c_vp, c_sz, c_i32, c_i32, c_vp]),
+    "ex_linear_partial_i64": (c_i32, [c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i32,
+                                      c_i32, c_vp, c_i64, c_vp, c_sz, c_i32, c_i32, c_vp]),
+    "ex_epilogue_i64": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_i64, c_vp]),
+    "ex_paged_decode_workspace_bytes": (c_sz, [c_i32, c_i32, c_i32, c_i32, c_i32]),
+    "ex_paged_decode": (c_i32, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_i32, c_i32,
+                                c_i32, c_i32, c_i32, c_f32, c_i32, c_i32, c_vp, c_i64, c_i64, c_i32, c_vp, c_sz,
+                                c_vp]),
+}
+
+_LIB = None
+
+
+class ExactError(RuntimeError):
+    """A C-ABI call returned a status other than EX_OK."""
+
+    def __init__(self, fn, status, detail=""):
+        self.status = status
+        super().__init__(f"{fn} failed with status {status}: {detail}")
+
+
+def lib():
+    """Load (once) and return the library; raises if it is missing."""
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"vllm-exact B200 library not found at {LIB_PATH}; build it with "
+                               "`python vllm-exact_b200/build.py` (there is no CPU fallback)")
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _LIB = L
+    return _LIB
+
+
+def check(fn_name, status):
+    if status != EX_OK:
+        L = lib()
+        detail = L.ex_status_string(status).decode()
+        if status == EX_ERR_CUDA:
+            detail += ": " + L.ex_last_error_string().decode()
+        raise ExactError(fn_name, status, detail)
+
+
+def device_error() -> int:
+    """Synchronize, return and clear the device error word (0 = no bounded wait timed out)."""
+    code = c_i32(0)
+    check("ex_device_error", lib().ex_device_error(ctypes.byref(code)))
+    return code.value

@@ -1,0 +1,141 @@
+"""vLLM quantization plugin quantization="exact_int8" on B200 (reference src/vllm_exact/plugin.py:1-133).
+
+Every linear layer (and lm_head unless disabled) runs the exact INT8 two-digit linear layer of kernels.py through a
+torch custom op ``exactmm::linear`` (same name and signature as the reference, plugin.py:51-69), whose body calls the
+sm_100a C ABI. No changes to vLLM source: register_quantization_config + the custom op. Imported and configured by
+vllm_exact.enable().
+
+Tensor parallelism: column-parallel layers (output-sharded: QKV, gate_up, GDN in_proj, vocab-parallel lm_head) hold
+full-K weight rows, so they need nothing special. Row-parallel layers (K-sharded: o_proj, down, GDN out_proj) go
+through parallel.py: global row scales (a MAX all-reduce of row maxima), an exact int64 partial GEMM on the local K
+slice, an int64 SUM all-reduce (exact under any reduction order) and the scaling epilogue. vLLM's own bf16
+all-reduce of that layer is switched off, because a sum of rounded partials is neither exact nor order-invariant.
+"""
+import json
+from pathlib import Path
+
+import torch
+
+from . import kernels as K
+from vllm.model_executor.layers.linear import LinearBase, RowParallelLinear, UnquantizedLinearMethod
+from vllm.model_executor.layers.quantization import register_quantization_config
+from vllm.model_executor.layers.quantization.base_config import QuantizationConfig
+from vllm.model_executor.layers.vocab_parallel_embedding import ParallelLMHead, UnquantizedEmbeddingMethod
+
+# set by enable()
+F = 14
+TRUNC = True
+LMHEAD = True
+_TABLE = None
+RB = 16384  # rows per block: rows are independent, results unchanged, temporary memory bounded (plugin.py:24)
+
+
+def load_table(path):
+    """Accepted for compatibility with the reference's tuning tables (plugin.py:27-34). The B200 kernels choose their
+    tiles from the shape; a table never changes results, so its contents are only recorded."""
+    global _TABLE
+    if path is None:
+        _TABLE = None
+        return
+    _TABLE = json.loads(Path(path).read_text())
+
+
+@torch.library.custom_op("exactmm::linear", mutates_args=())
+def exact_linear_op(x: torch.Tensor, wh: torch.Tensor, wl: torch.Tensor, cw: torch.Tensor,
+                    sw: torch.Tensor) -> torch.Tensor:
+    shp = x.shape
+    N = wh.shape[0]
+    x2 = x.reshape(-1, shp[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    M = x2.shape[0]
+    out = x.new_empty(M, N)
+    for i in range(0, M, RB):
+        xb = x2[i:i + RB]
+        xd = K.digitize(xb, F)  # reads bf16 directly (bf16 -> fp32 is exact, same digits)
+        K.exact_linear(xd, (wh, wl, cw, sw), F, TRUNC, out=out[i:i + RB])  # writes bf16 directly
+    return out.reshape(*shp[:-1], N)
+
+
+@exact_linear_op.register_fake
+def _(x, wh, wl, cw, sw):
+    return x.new_empty(*x.shape[:-1], wh.shape[0])
+
+
+def _is_row_sharded(layer) -> bool:
+    return isinstance(layer, RowParallelLinear) and getattr(layer, "tp_size", 1) > 1
+
+
+def _digitize_layer(layer):
+    """Digitize the weight once after loading into non-persistent buffers ex_wh / ex_wl (int8, rows padded to 16
+    bytes for TMA) and ex_cw / ex_sw (int32) (reference plugin.py:72-79)."""
+    w = layer.weight.data
+    if _is_row_sharded(layer):
+        from . import parallel
+        h, l, cs, sh = parallel.digitize_weight_row_sharded(w, F)
+    else:
+        h, l, cs, sh = K.digitize_weight(w, F)
+    layer.register_buffer("ex_wh", h, persistent=False)
+    layer.register_buffer("ex_wl", l, persistent=False)
+    layer.register_buffer("ex_cw", cs.contiguous(), persistent=False)
+    layer.register_buffer("ex_sw", sh.contiguous(), persistent=False)
+    if _is_row_sharded(layer):
+        layer.reduce_results = False  # the exact int64 all-reduce inside apply replaces vLLM's bf16 all-reduce
+
+
+def _apply(layer, x, bias):
+    if _is_row_sharded(layer):
+        from . import parallel
+        y = parallel.row_parallel_linear(x, layer.ex_wh, layer.ex_wl, layer.ex_cw, layer.ex_sw, F, TRUNC)
+    else:
+        y = torch.ops.exactmm.linear(x, layer.ex_wh, layer.ex_wl, layer.ex_cw, layer.ex_sw)
+    return y if bias is None else y + bias
+
+
+class ExactLinearMethod(UnquantizedLinearMethod):
+    def process_weights_after_loading(self, layer: torch.nn.Module) -> None:
+        _digitize_layer(layer)
+
+    def apply(self, layer, x, bias=None):
+        return _apply(layer, x, bias)
+
+
+class ExactLMHeadMethod(UnquantizedEmbeddingMethod):
+    """lm_head through the exact linear layer. lm_head does no embedding lookup; the parent embedding() is kept."""
+
+    def process_weights_after_loading(self, layer: torch.nn.Module) -> None:
+        _digitize_layer(layer)
+
+    def apply(self, layer, x, bias=None):
+        return _apply(layer, x, bias)
+
+
+@register_quantization_config("exact_int8")
+class ExactInt8Config(QuantizationConfig):
+    def __init__(self):
+        super().__init__()
+
+    def get_name(self):
+        return "exact_int8"
+
+    def get_supported_act_dtypes(self):
+        return [torch.bfloat16, torch.float16]
+
+    @classmethod
+    def get_min_capability(cls):
+        return 100  # the kernels are built for sm_100a only
+
+    @staticmethod
+    def get_config_filenames():
+        return []
+
+    @classmethod
+    def from_config(cls, config):
+        return cls()
+
+    def get_quant_method(self, layer, prefix):
+        if isinstance(layer, LinearBase):
+            return ExactLinearMethod()
+        if LMHEAD and isinstance(layer, ParallelLMHead):
+            return ExactLMHeadMethod()
+        return None
