@@ -1,0 +1,377 @@
+"""Benchmark of vllm-exact B200: exact_int8 GEMM throughput against the roofline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload ("step"): the decode part of the BASELINE configs[1] sweep on one B200 -- for M in {1, 16, 64} and
+each (K, N) in {QKV (4096, 6144), O-proj (4096, 4096), gate_up (4096, 24576), down (12288, 4096), lm_head
+(4096, 151936)}: bf16 activations -> digitize -> exact two-digit GEMM -> bf16 output (the exactmm::linear op).
+value = algorithmic HBM bytes of the 15 GEMMs (weight digits 2NK + weight scales 4N + activation digits 2MK + row
+scales 4M + bf16 output 2MN) / device time of the step, in TB/s. Weights of one (K, N) are re-used only after the four
+other matrices (>= 1.5 GB) went through the 126 MB L2, so every step streams its weights from HBM.
+
+Also reported (not part of `value`): the tensor-bound sweep M in {256, 4096} as TFLOP/s of executed digit-product
+flops (6 M N K) against the measured bf16 dense peak, the paged decode attention of configs[3], the end-to-end rate
+through the public op with host copies, the CPU oracle on a bounded sample, and the SM clocks during the run.
+
+--impl reference times the reference's CPU integer path (restated in oracle/, numpy) on a bounded sample of the same
+workload with all host threads, and prints the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for p in (ROOT, ROOT / "vllm-exact_b200", ROOT / "tests" / "golden"):
+    if str(p) not in sys.path:
+        sys.path.insert(0, str(p))
+
+SHAPES = [("qkv", 4096, 6144), ("o_proj", 4096, 4096), ("gate_up", 4096, 24576), ("down", 12288, 4096),
+          ("lm_head", 4096, 151936)]
+DECODE_M = [1, 16, 64]
+TENSOR_M = [256, 4096]
+ATTN = [(256, 1024), (64, 8192), (16, 16384)]
+METRIC = "exact-GEMM TB/s (exact_int8 linear, decode shapes M<=64 of the configs[1] sweep)"
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def gemm_bytes(M, K, N):
+    return 2 * N * K + 4 * N + 2 * M * K + 4 * M + 2 * M * N
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ------------------------------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# our arm
+# ------------------------------------------------------------------------------------------------------------------
+def make_activation(M, K, seed, dev):
+    import torch
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(M, K, generator=g, device=dev)
+    x[torch.rand(M, K, generator=g, device=dev) < 0.001] *= 50
+    return x.bfloat16()
+
+
+def make_weight_digits(K, N, seed, dev, F=14):
+    """Weights ~N(0, 0.02) in bf16, digitized at load time like the plugin (kernels.digitize_weight)."""
+    import torch
+    from vllm_exact import kernels as KK
+    g = torch.Generator(device=dev).manual_seed(seed)
+    out = KK._alloc_digits(N, K, dev)
+    for i in range(0, N, 16384):
+        j = min(N, i + 16384)
+        w = (torch.randn(j - i, K, generator=g, device=dev) * 0.02).bfloat16()
+        KK.digitize(w, F, out=tuple(t[i:j] for t in out))
+    return out
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from vllm_exact import kernels as KK, paged_attn as PA
+    import vllm_exact.ops  # noqa: F401  (registers exactmm::linear without importing vLLM)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    hbm, bf16_burst, bf16_sust, peak_kind = peaks()
+
+    # ---------------- workload: weights resident in HBM, activations per (M, shape)
+    W = {name: make_weight_digits(K, N, 1000 + i, dev) for i, (name, K, N) in enumerate(SHAPES)}
+    X = {(M, name): make_activation(M, K, 17 * M + i, dev) for M in DECODE_M for i, (name, K, N) in enumerate(SHAPES)}
+    Y = {(M, name): torch.empty(M, N, device=dev, dtype=torch.bfloat16) for M in DECODE_M for name, K, N in SHAPES}
+    order = [(M, name, K, N) for M in DECODE_M for name, K, N in SHAPES]
+    step_bytes = sum(gemm_bytes(M, K, N) for M, name, K, N in order)
+    # the workspace for split tiles, sized for the largest plan, before timing
+    KK.reserve_workspace(max(KK.lib().ex_linear_workspace_bytes(M, N, K, 0, 0) for M, _, K, N in order), dev)
+    stream = torch.cuda.current_stream(dev)
+    launches = {"n": 0}
+
+    def one_step(ev=None):
+        for i, (M, name, K, N) in enumerate(order):
+            xd = KK.digitize(X[(M, name)], 14)
+            if ev is not None:
+                ev[i][0].record(stream)
+            KK.exact_linear(xd, W[name], 14, True, out=Y[(M, name)])
+            if ev is not None:
+                ev[i][1].record(stream)
+            launches["n"] += 2
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in order]
+           for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches["n"] = 0
+    with ClockSampler(local) as clk:
+        t0.record(stream)
+        for s in range(args.steps):
+            one_step(evs[s])
+        t1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt)
+    gemm_ms = sum(a.elapsed_time(b) for step in evs for a, b in step)
+    per_gemm = {}
+    for i, (M, name, K, N) in enumerate(order):
+        us = 1000 * statistics.median(evs[s][i][0].elapsed_time(evs[s][i][1]) for s in range(args.steps))
+        per_gemm[f"{name}/M{M}"] = {"us": round(us, 2), "GBps": round(gemm_bytes(M, K, N) / us / 1e3, 1),
+                                    "frac_hbm": round(gemm_bytes(M, K, N) / us / 1e3 / hbm, 3)}
+    ms_per_step = ms / args.steps
+    value = world * step_bytes / (ms_per_step * 1e-3) / 1e12
+    achieved = args.steps * step_bytes / (gemm_ms * 1e-3) / 1e9  # GB/s over GEMM launches only
+
+    result = {
+        "metric": METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8 digits (exact int32/int64), bf16 in/out", "data": "synthetic",
+        "config": {"workload": "configs[1] decode sweep: M in {1,16,64} x (K,N) in {(4096,6144),(4096,4096),"
+                               "(4096,24576),(12288,4096),(4096,151936)}, F=14 truncated, bf16 out",
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2: 1.63 GB of weight digits rotated between re-uses of a matrix",
+                   "per_step_bytes": step_bytes},
+        "gpu_launches": launches["n"],
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 4), "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "k_exact_tc_i8 (all 15 decode GEMM launches; algorithmic bytes / summed durations)"},
+        "sweep_decode": per_gemm,
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        result["sweep_tensor"] = tensor_sweep(dev, W, bf16_burst, args.quick)
+        result["attention"] = attention_bench(dev, hbm, args.quick)
+        result["e2e"] = e2e_bench(dev, W, order, args)
+        if world == 1 and not args.quick:
+            result["cpu_baseline"] = cpu_baseline(W)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def _time(fn, reps, warm=2):
+    import torch
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def tensor_sweep(dev, W, peak_bf16, quick):
+    import torch
+    from vllm_exact import kernels as KK
+    out = {}
+    for M in TENSOR_M:
+        for i, (name, K, N) in enumerate(SHAPES):
+            if quick and M > 256:
+                continue
+            x = make_activation(M, K, 7 * M + i, dev)
+            xd = KK.digitize(x, 14)
+            y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            KK.reserve_workspace(KK.lib().ex_linear_workspace_bytes(M, N, K, 0, 0), dev)
+            ms = _time(lambda: KK.exact_linear(xd, W[name], 14, True, out=y), 3 if M > 256 else 10)
+            fl = 6.0 * M * N * K
+            out[f"{name}/M{M}"] = {"us": round(ms * 1e3, 1), "TFLOPs_executed": round(fl / ms / 1e9, 1),
+                                   "frac_bf16_peak": round(fl / ms / 1e9 / peak_bf16, 3),
+                                   "TFLOPs_useful": round(fl / 3 / ms / 1e9, 1)}
+    return out
+
+
+def attention_bench(dev, hbm, quick):
+    import torch
+    import recipes as R
+    from vllm_exact import paged_attn as PA
+    PA.MAX_LEN = 20480
+    res = {}
+    for n, ctx in ATTN:
+        q, kv, bt, sl = R.paged_case(n, ctx, 16, 32, 8, 128, ctx_jitter=True)
+        q, kv, bt, sl = q.to(dev), kv.to(dev), bt.to(dev), sl.to(dev)
+        kc, vc = R.kv_views(kv, 128)
+        o = torch.empty(n, 32, 128, device=dev, dtype=torch.bfloat16)
+        ws = torch.empty(PA.workspace_bytes(n, 32, 128), dtype=torch.uint8, device=dev)
+        ms = _time(lambda: PA.paged_decode(q, kc, vc, bt, sl, 128 ** -0.5, o, n, workspace=ws), 5 if quick else 20)
+        L = int(sl.sum())
+        by = L * 8 * 128 * 2 * 2 + 2 * n * 32 * 128 * 2 + sum((int(l) + 15) // 16 for l in sl.tolist()) * 4 + 4 * n
+        res[f"b{n}/{ctx // 1024}K"] = {"us": round(ms * 1e3, 1), "GBps": round(by / ms / 1e6, 1),
+                                       "frac_hbm": round(by / ms / 1e6 / hbm, 3), "bytes": by}
+        del kv
+    return res
+
+
+def e2e_bench(dev, W, order, args):
+    """Same decode sweep through the public op exactmm::linear with host buffers: per GEMM, the activations are
+    copied from pinned host memory and the bf16 result read back, inside the timed region."""
+    import torch
+    H = {(M, name): make_activation(M, K, 17 * M + i, dev).cpu().pin_memory()
+         for M in DECODE_M for i, (name, K, N) in enumerate(SHAPES)}
+    O = {(M, name): torch.empty(M, N, dtype=torch.bfloat16).pin_memory() for M, name, K, N in order}
+    h2d = sum(M * K * 2 for M, name, K, N in order)
+    d2h = sum(M * N * 2 for M, name, K, N in order)
+    by = sum(gemm_bytes(M, K, N) for M, name, K, N in order)
+
+    def step():
+        for M, name, K, N in order:
+            x = H[(M, name)].to(dev, non_blocking=True)
+            y = torch.ops.exactmm.linear(x, *W[name][:2], W[name][2], W[name][3])
+            O[(M, name)].copy_(y, non_blocking=True)
+
+    ms = _time(step, max(3, args.steps // 2), warm=max(2, args.warmup))
+    return {"value": round(by / (ms * 1e-3) / 1e12, 4), "unit": "TB/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 4), "api": "torch.ops.exactmm.linear"}
+
+
+def cpu_baseline(W=None, budget_s=20.0):
+    """The reference's CPU integer path, restated in oracle/ (numpy; integer dot products as exact float64 BLAS
+    products), on a bounded sample of the decode sweep: every (M, shape) with the output columns capped at 2048
+    (output columns are independent). Same metric: algorithmic bytes of the sampled GEMMs / time."""
+    import numpy as np
+    from oracle import exact_oracle as O
+    threads = os.cpu_count()
+    rng = np.random.default_rng(0)
+    ncap = 2048
+    tot_bytes, tot_s, runs = 0, 0.0, 0
+    t_start = time.perf_counter()
+    while time.perf_counter() - t_start < budget_s and runs < 3:
+        for M in DECODE_M:
+            for name, K, N in SHAPES:
+                n = min(N, ncap)
+                w = (rng.standard_normal((n, K), dtype=np.float32) * 0.02)
+                x = rng.standard_normal((M, K), dtype=np.float32)
+                t = time.perf_counter()
+                wd = O.digitize(w, 14)
+                y = O.exact_linear(O.digitize(x, 14), wd, 14, True)
+                O.f32_to_bf16_bits(y)
+                tot_s += time.perf_counter() - t
+                tot_bytes += gemm_bytes(M, K, n)
+        runs += 1
+    return {"value": round(tot_bytes / tot_s / 1e12, 6), "unit": "TB/s", "cores": threads, "kind": "port",
+            "sample": f"{runs} pass(es) of the 15 decode GEMMs with N capped at {ncap} output columns "
+                      f"(digitize + exact integer GEMM + bf16), numpy oracle, {threads} host threads",
+            "seconds": round(tot_s, 2)}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np  # noqa: F401
+    per = [cpu_baseline(budget_s=max(5.0, 60.0 / max(1, args.steps + args.warmup))) for _ in range(1)]
+    v = per[0]["value"]
+    print(json.dumps({
+        "metric": METRIC, "value": v, "unit": "TB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": None, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int64 (CPU)", "data": "synthetic", "impl": "reference",
+        "config": {"workload": "configs[1] decode sweep, bounded CPU sample", "parallelism": "cpu"},
+        "cpu_baseline": per[0], "e2e": {"value": v, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--quick", action="store_true", help="skip the slow secondary measurements")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

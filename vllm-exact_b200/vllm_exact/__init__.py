@@ -44,9 +44,9 @@ def enable(max_model_len, f=14, lm_head=True, attention=True, cfg_table="b200", 
     os.environ["VLLM_BATCH_INVARIANT"] = "1"
     os.environ["VLLM_ENABLE_V1_MULTIPROCESSING"] = "0"
 
-    from . import plugin  # registers exact_int8 (first import of vllm happens here)
-    plugin.F = f
-    plugin.TRUNC = f == 14
+    from . import ops, plugin  # registers exact_int8 (first import of vllm happens here)
+    plugin.F = ops.F = f
+    plugin.TRUNC = ops.TRUNC = f == 14
     plugin.LMHEAD = lm_head
     plugin.load_table(TABLES.get(cfg_table, cfg_table) if cfg_table else None)
 

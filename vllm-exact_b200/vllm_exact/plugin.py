@@ -1,8 +1,8 @@
 """vLLM quantization plugin quantization="exact_int8" on B200 (reference src/vllm_exact/plugin.py:1-133).
 
-Every linear layer (and lm_head unless disabled) runs the exact INT8 two-digit linear layer of kernels.py through a
-torch custom op ``exactmm::linear`` (same name and signature as the reference, plugin.py:51-69), whose body calls the
-sm_100a C ABI. No changes to vLLM source: register_quantization_config + the custom op. Imported and configured by
+Every linear layer (and lm_head unless disabled) runs the exact INT8 two-digit linear layer of kernels.py through the
+torch custom op ``exactmm::linear`` of ops.py (same name and signature as the reference, plugin.py:51-69), whose body
+calls the sm_100a C ABI. No changes to vLLM source: register_quantization_config + the custom op. Imported and configured by
 vllm_exact.enable().
 
 Tensor parallelism: column-parallel layers (output-sharded: QKV, gate_up, GDN in_proj, vocab-parallel lm_head) hold
@@ -17,17 +17,18 @@ from pathlib import Path
 import torch
 
 from . import kernels as K
+from . import ops
 from vllm.model_executor.layers.linear import LinearBase, RowParallelLinear, UnquantizedLinearMethod
 from vllm.model_executor.layers.quantization import register_quantization_config
 from vllm.model_executor.layers.quantization.base_config import QuantizationConfig
 from vllm.model_executor.layers.vocab_parallel_embedding import ParallelLMHead, UnquantizedEmbeddingMethod
 
-# set by enable()
+# set by enable() (which also sets ops.F / ops.TRUNC, read by the custom op)
 F = 14
 TRUNC = True
 LMHEAD = True
 _TABLE = None
-RB = 16384  # rows per block: rows are independent, results unchanged, temporary memory bounded (plugin.py:24)
+RB = ops.RB  # rows per block: rows are independent, results unchanged, temporary memory bounded (plugin.py:24)
 
 
 def load_table(path):
@@ -38,28 +39,6 @@ def load_table(path):
         _TABLE = None
         return
     _TABLE = json.loads(Path(path).read_text())
-
-
-@torch.library.custom_op("exactmm::linear", mutates_args=())
-def exact_linear_op(x: torch.Tensor, wh: torch.Tensor, wl: torch.Tensor, cw: torch.Tensor,
-                    sw: torch.Tensor) -> torch.Tensor:
-    shp = x.shape
-    N = wh.shape[0]
-    x2 = x.reshape(-1, shp[-1])
-    if x2.stride(-1) != 1:
-        x2 = x2.contiguous()
-    M = x2.shape[0]
-    out = x.new_empty(M, N)
-    for i in range(0, M, RB):
-        xb = x2[i:i + RB]
-        xd = K.digitize(xb, F)  # reads bf16 directly (bf16 -> fp32 is exact, same digits)
-        K.exact_linear(xd, (wh, wl, cw, sw), F, TRUNC, out=out[i:i + RB])  # writes bf16 directly
-    return out.reshape(*shp[:-1], N)
-
-
-@exact_linear_op.register_fake
-def _(x, wh, wl, cw, sw):
-    return x.new_empty(*x.shape[:-1], wh.shape[0])
 
 
 def _is_row_sharded(layer) -> bool:
