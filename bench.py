@@ -81,6 +81,11 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def wait_first_sample(self, timeout=5.0):
+        t = time.time()
+        while self.proc is not None and not self.lines and time.time() - t < timeout:
+            time.sleep(0.02)
+
     def __exit__(self, *a):
         if self.proc is not None:
             self.proc.terminate()
@@ -158,34 +163,59 @@ def run_ours(args):
     step_bytes = sum(gemm_bytes(M, K, N) for M, name, K, N in order)
     # the workspace for split tiles, sized for the largest plan, before timing
     KK.reserve_workspace(max(KK.lib().ex_linear_workspace_bytes(M, N, K, 0, 0) for M, _, K, N in order), dev)
-    stream = torch.cuda.current_stream(dev)
-    launches = {"n": 0}
+    stream = torch.cuda.Stream(dev)
+    KK.reserve_workspace(max(KK.lib().ex_linear_workspace_bytes(M, N, K, 0, 0) for M, _, K, N in order), dev,
+                         stream=stream)
 
     def one_step(ev=None):
+        n = 0
         for i, (M, name, K, N) in enumerate(order):
             xd = KK.digitize(X[(M, name)], 14)
             if ev is not None:
-                ev[i][0].record(stream)
+                ev[i][0].record()
             KK.exact_linear(xd, W[name], 14, True, out=Y[(M, name)])
             if ev is not None:
-                ev[i][1].record(stream)
-            launches["n"] += 2
+                ev[i][1].record()
+            n += 2
+        return n
 
+    # CUDA graphs, as vLLM runs decode: graph A = one step; graphs B_r = one step with timing events around each GEMM
+    R = min(10, args.steps)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            one_step()
+    torch.cuda.synchronize()
+    gA = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gA, stream=stream):
+        launches_per_step = one_step()
+    evB = [[[torch.cuda.Event(enable_timing=True, external=True) for _ in range(2)] for _ in order] for _ in range(R)]
+    gB = []
+    for r in range(R):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            one_step(evB[r])
+        gB.append(g)
     for _ in range(args.warmup):
-        one_step()
+        gA.replay()
     torch.cuda.synchronize()
-    evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in order]
-           for _ in range(args.steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    launches["n"] = 0
+    t2, t3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
-        t0.record(stream)
-        for s in range(args.steps):
-            one_step(evs[s])
-        t1.record(stream)
+        clk.wait_first_sample()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            t0.record()
+            for _ in range(args.steps):
+                gA.replay()
+            t1.record()
+            # per-GEMM durations from the last R steps of a second timed pass
+            t2.record()
+            for _ in range(max(args.steps // R, 1)):
+                for g in gB:
+                    g.replay()
+            t3.record()
         torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -194,15 +224,17 @@ def run_ours(args):
         tt = torch.tensor([ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt)
-    gemm_ms = sum(a.elapsed_time(b) for step in evs for a, b in step)
+    ms_events = t2.elapsed_time(t3) / (max(args.steps // R, 1) * R)
+    gemm_ms = sum(a.elapsed_time(b) for step in evB for a, b in step)
     per_gemm = {}
     for i, (M, name, K, N) in enumerate(order):
-        us = 1000 * statistics.median(evs[s][i][0].elapsed_time(evs[s][i][1]) for s in range(args.steps))
+        us = 1000 * statistics.median(evB[r][i][0].elapsed_time(evB[r][i][1]) for r in range(R))
         per_gemm[f"{name}/M{M}"] = {"us": round(us, 2), "GBps": round(gemm_bytes(M, K, N) / us / 1e3, 1),
                                     "frac_hbm": round(gemm_bytes(M, K, N) / us / 1e3 / hbm, 3)}
     ms_per_step = ms / args.steps
     value = world * step_bytes / (ms_per_step * 1e-3) / 1e12
-    achieved = args.steps * step_bytes / (gemm_ms * 1e-3) / 1e9  # GB/s over GEMM launches only
+    achieved = R * step_bytes / (gemm_ms * 1e-3) / 1e9  # GB/s over the GEMM launches only
+    launches = {"n": launches_per_step * args.steps}
 
     result = {
         "metric": METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
@@ -212,7 +244,9 @@ def run_ours(args):
                                "(4096,24576),(12288,4096),(4096,151936)}, F=14 truncated, bf16 out",
                    "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2: 1.63 GB of weight digits rotated between re-uses of a matrix",
-                   "per_step_bytes": step_bytes},
+                   "per_step_bytes": step_bytes, "timing": "CUDA graph of one step (15 x digitize + GEMM), "
+                   "replayed --steps times; per-GEMM durations from timing events captured in the graphs",
+                   "ms_per_step_with_timing_events": round(ms_events, 4)},
         "gpu_launches": launches["n"],
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": None, "peak_kind": peak_kind,
@@ -233,64 +267,95 @@ def run_ours(args):
         print(json.dumps(result), flush=True)
 
 
-def _time(fn, reps, warm=2):
+def _graph_time(fns, reps, stream, warm=2):
+    """Capture `fns` (a list of launch callables) into one CUDA graph with external timing events around each, replay
+    it `reps` times, and return (ms per replay, [median ms of each fn])."""
     import torch
-    for _ in range(warm):
-        fn()
+    with torch.cuda.stream(stream):
+        for _ in range(warm):
+            for f in fns:
+                f()
+    torch.cuda.synchronize()
+    ev = [[[torch.cuda.Event(enable_timing=True, external=True) for _ in range(2)] for _ in fns]
+          for _ in range(reps)]
+    graphs = []
+    for r in range(reps):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i, f in enumerate(fns):
+                ev[r][i][0].record()
+                f()
+                ev[r][i][1].record()
+        graphs.append(g)
+    graphs[0].replay()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(reps):
-        fn()
-    b.record()
+    with torch.cuda.stream(stream):
+        a.record()
+        for g in graphs:
+            g.replay()
+        b.record()
     torch.cuda.synchronize()
-    return a.elapsed_time(b) / reps
+    per = [statistics.median(ev[r][i][0].elapsed_time(ev[r][i][1]) for r in range(reps)) for i in range(len(fns))]
+    del graphs
+    return a.elapsed_time(b) / reps, per
 
 
 def tensor_sweep(dev, W, peak_bf16, quick):
+    """M in {256, 4096}: one graph per M with the five shapes in sequence (weights rotate through L2)."""
     import torch
     from vllm_exact import kernels as KK
+    stream = torch.cuda.Stream(dev)
     out = {}
     for M in TENSOR_M:
-        for i, (name, K, N) in enumerate(SHAPES):
-            if quick and M > 256:
-                continue
-            x = make_activation(M, K, 7 * M + i, dev)
-            xd = KK.digitize(x, 14)
-            y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
-            KK.reserve_workspace(KK.lib().ex_linear_workspace_bytes(M, N, K, 0, 0), dev)
-            ms = _time(lambda: KK.exact_linear(xd, W[name], 14, True, out=y), 3 if M > 256 else 10)
+        if quick and M > 256:
+            continue
+        xs = {name: KK.digitize(make_activation(M, K, 7 * M + i, dev), 14) for i, (name, K, N) in enumerate(SHAPES)}
+        ys = {name: torch.empty(M, N, device=dev, dtype=torch.bfloat16) for name, K, N in SHAPES}
+        KK.reserve_workspace(max(KK.lib().ex_linear_workspace_bytes(M, N, K, 0, 0) for _, K, N in SHAPES), dev,
+                             stream=stream)
+        fns = [(lambda name=name: KK.exact_linear(xs[name], W[name], 14, True, out=ys[name])) for name, K, N in SHAPES]
+        _, per = _graph_time(fns, 3 if M > 256 else 10, stream)
+        for (name, K, N), ms in zip(SHAPES, per):
             fl = 6.0 * M * N * K
             out[f"{name}/M{M}"] = {"us": round(ms * 1e3, 1), "TFLOPs_executed": round(fl / ms / 1e9, 1),
                                    "frac_bf16_peak": round(fl / ms / 1e9 / peak_bf16, 3),
                                    "TFLOPs_useful": round(fl / 3 / ms / 1e9, 1)}
+        del xs, ys
     return out
 
 
 def attention_bench(dev, hbm, quick):
+    """H=32, KV=8, D=128, page 16, lengths +-25%; one graph with the three batches in sequence."""
     import torch
     import recipes as R
     from vllm_exact import paged_attn as PA
     PA.MAX_LEN = 20480
-    res = {}
+    stream = torch.cuda.Stream(dev)
+    cases, fns = [], []
     for n, ctx in ATTN:
         q, kv, bt, sl = R.paged_case(n, ctx, 16, 32, 8, 128, ctx_jitter=True)
         q, kv, bt, sl = q.to(dev), kv.to(dev), bt.to(dev), sl.to(dev)
         kc, vc = R.kv_views(kv, 128)
         o = torch.empty(n, 32, 128, device=dev, dtype=torch.bfloat16)
         ws = torch.empty(PA.workspace_bytes(n, 32, 128), dtype=torch.uint8, device=dev)
-        ms = _time(lambda: PA.paged_decode(q, kc, vc, bt, sl, 128 ** -0.5, o, n, workspace=ws), 5 if quick else 20)
         L = int(sl.sum())
         by = L * 8 * 128 * 2 * 2 + 2 * n * 32 * 128 * 2 + sum((int(l) + 15) // 16 for l in sl.tolist()) * 4 + 4 * n
+        cases.append((n, ctx, by, (q, kv, bt, sl, o, ws)))
+        fns.append(lambda q=q, kc=kc, vc=vc, bt=bt, sl=sl, o=o, ws=ws, n=n:
+                   PA.paged_decode(q, kc, vc, bt, sl, 128 ** -0.5, o, n, workspace=ws))
+    _, per = _graph_time(fns, 5 if quick else 20, stream)
+    res = {}
+    for (n, ctx, by, _), ms in zip(cases, per):
         res[f"b{n}/{ctx // 1024}K"] = {"us": round(ms * 1e3, 1), "GBps": round(by / ms / 1e6, 1),
                                        "frac_hbm": round(by / ms / 1e6 / hbm, 3), "bytes": by}
-        del kv
     return res
 
 
 def e2e_bench(dev, W, order, args):
     """Same decode sweep through the public op exactmm::linear with host buffers: per GEMM, the activations are
-    copied from pinned host memory and the bf16 result read back, inside the timed region."""
+    copied from pinned host memory and the bf16 result is read back into pinned host memory, inside the timed region
+    (one CUDA graph per step, as vLLM captures decode)."""
     import torch
     H = {(M, name): make_activation(M, K, 17 * M + i, dev).cpu().pin_memory()
          for M in DECODE_M for i, (name, K, N) in enumerate(SHAPES)}
@@ -298,16 +363,35 @@ def e2e_bench(dev, W, order, args):
     h2d = sum(M * K * 2 for M, name, K, N in order)
     d2h = sum(M * N * 2 for M, name, K, N in order)
     by = sum(gemm_bytes(M, K, N) for M, name, K, N in order)
+    stream = torch.cuda.Stream(dev)
 
     def step():
         for M, name, K, N in order:
             x = H[(M, name)].to(dev, non_blocking=True)
-            y = torch.ops.exactmm.linear(x, *W[name][:2], W[name][2], W[name][3])
+            y = torch.ops.exactmm.linear(x, W[name][0], W[name][1], W[name][2], W[name][3])
             O[(M, name)].copy_(y, non_blocking=True)
 
-    ms = _time(step, max(3, args.steps // 2), warm=max(2, args.warmup))
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        step()
+    reps = max(3, args.steps // 4)
+    for _ in range(args.warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
     return {"value": round(by / (ms * 1e-3) / 1e12, 4), "unit": "TB/s", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 4), "api": "torch.ops.exactmm.linear"}
+            "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 4),
+            "api": "torch.ops.exactmm.linear (pinned host in, pinned host out), CUDA graph per step"}
 
 
 def cpu_baseline(W=None, budget_s=20.0):
@@ -357,14 +441,51 @@ def run_reference(args):
     }), flush=True)
 
 
+def run_case(args):
+    """Small single-kernel workloads for ncu captures: `gemm:<shape>:<M>[:<algo>]` or `attn:<n>:<ctx>`; runs the
+    kernel --reps times eagerly (ncu flushes caches before each captured pass)."""
+    import torch
+    from vllm_exact import kernels as KK, paged_attn as PA
+    import recipes as R
+    dev = torch.device("cuda", 0)
+    kind, *rest = args.case.split(":")
+    if kind == "gemm":
+        name, M = rest[0], int(rest[1])
+        algo = {"tc_i8": KK.EX_ALGO_TC_I8, "simt": KK.EX_ALGO_SIMT, "auto": KK.EX_ALGO_AUTO}[rest[2] if len(rest) > 2
+                                                                                            else "auto"]
+        (K, N), = [(k, n) for nm, k, n in SHAPES if nm == name]
+        W = make_weight_digits(K, N, 1, dev)
+        xd = KK.digitize(make_activation(M, K, 2, dev), 14)
+        y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        for _ in range(args.reps):
+            KK.exact_linear(xd, W, 14, True, out=y, cfg={"algo": algo})
+    elif kind == "attn":
+        n, ctx = int(rest[0]), int(rest[1])
+        PA.MAX_LEN = 20480
+        q, kv, bt, sl = [t.to(dev) for t in R.paged_case(n, ctx, 16, 32, 8, 128, ctx_jitter=True)]
+        kc, vc = R.kv_views(kv, 128)
+        o = torch.empty(n, 32, 128, device=dev, dtype=torch.bfloat16)
+        for _ in range(args.reps):
+            PA.paged_decode(q, kc, vc, bt, sl, 128 ** -0.5, o, n)
+    else:
+        raise SystemExit(f"unknown case {args.case}")
+    torch.cuda.synchronize()
+    print(f"case {args.case} done")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--quick", action="store_true", help="skip the slow secondary measurements")
+    ap.add_argument("--case", default=None, help="profiling workload, e.g. gemm:o_proj:64 or attn:64:8192")
+    ap.add_argument("--reps", type=int, default=3)
     args = ap.parse_args()
+    if args.case:
+        run_case(args)
+        return
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":

@@ -123,7 +123,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
 
 // ------------------------------------------------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor), tiled 2D loads into this CTA's shared memory, completion counted on an mbarrier.
-// Loads only: no store/reduce forms, and no cluster-wide forms are used anywhere in this library.
+// Tensor loads into this CTA only; no cluster-wide forms are used anywhere in this library.
 // ------------------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             uint64_t cache_hint) {
@@ -245,6 +245,29 @@ __device__ __forceinline__ uint32_t elect_one() {
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(pred));
   return pred;
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// bulk (TMA-engine) reduce-add of a shared-memory buffer into global memory, tracked with bulk groups
+// ------------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void bulk_reduce_add_u64(void* gdst, const void* ssrc, uint32_t bytes) {
+  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.u64 [%0], [%1], %2;" ::"l"(gdst),
+               "r"(ex_smem_u32(ssrc)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the shared-memory source of all but the newest N bulk groups may be overwritten
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// every bulk group of this thread has completed (its global writes are performed)
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 // ------------------------------------------------------------------------------------------------------------------

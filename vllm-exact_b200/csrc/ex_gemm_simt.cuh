@@ -138,9 +138,11 @@ __global__ void __launch_bounds__(SIMT_THREADS) k_exact_simt(
   if (!s_last) return;
   __threadfence();
   if (n < N) {
+#pragma unroll 4
     for (int m = 0; m < M; ++m) {
-      const long long tot =
-          (long long)atomicExch(reinterpret_cast<unsigned long long*>(ws_acc + (int64_t)m * N + n), 0ull);
+      long long* p = ws_acc + (int64_t)m * N + n;
+      const long long tot = __ldcg(p);  // every other contribution is in L2; this CTA owns the row block now
+      __stcg(p, 0ll);
       ex_finish<F, OUT_DTYPE, PARTIAL>(tot, m, n, K, cx, cw, sx, sw, out, ldo);
     }
   }

@@ -21,8 +21,9 @@
 // Work partition: the (tile, k-iteration) space is flattened (tiles ordered n-major, m-minor so the m-tiles that
 // share a weight tile run back to back) and cut into G equal contiguous ranges, one per CTA. A CTA's range is a list
 // of segments (tile, k_begin, k_end). A segment covering a whole tile is written directly; otherwise its int64
-// totals are added into a workspace with relaxed atomics and a per-tile ticket counting k-iterations elects the CTA
-// that completes the tile, which applies the epilogue and zeroes the workspace again. Integer addition is exact and
+// totals are added with relaxed atomics into the tile's workspace slot (at most G - 1 tiles are split, one slot per
+// CTA boundary) and a ticket counting k-iterations elects the CTA that completes the tile, which applies the
+// epilogue and zeroes the slot again. Integer addition is exact and
 // order-free, so the result bits do not depend on G, on the split, or on arrival order.
 #pragma once
 #include "ex_common.cuh"
@@ -35,6 +36,8 @@ constexpr int TC_BK = 128;               // K bytes (int8 elements) per pipeline
 constexpr int TC_WTILE = 128 * TC_BK;    // bytes of one weight digit tile
 constexpr int TC_SMEM_BUDGET = 220 * 1024;
 constexpr int TC_TMEM_COLS = 512;
+constexpr int TC_RED_TOK = 8;                                // tokens per bulk reduce-add (2 KB per warp)
+constexpr int TC_RED_STAGING = 4 * 2 * TC_RED_TOK * 32 * 8;  // 4 warps x 2 buffers x 8 tokens x 32 rows x int64
 
 struct TcPlan {
   int BT;        // token tile
@@ -130,7 +133,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // 1024-byte alignment for the 128-byte-swizzled tiles
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = a.stages;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + (size_t)S * Lay::STAGE);
+  // per epilogue warp, two 2 KB staging buffers (8 tokens x 32 rows of int64) for bulk reduce-adds of split tiles
+  long long* stage_red = reinterpret_cast<long long*>(smem + (size_t)S * Lay::STAGE);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + (size_t)S * Lay::STAGE + TC_RED_STAGING);
   uint64_t* empty_bar = full_bar + S;
   uint64_t* tfull_bar = empty_bar + S;   // [2]
   uint64_t* tempty_bar = tfull_bar + 2;  // [2]
@@ -215,6 +220,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         mbar_wait(full_bar + stage, phase, EX_DEVERR_WAIT_TMA);
       }
     }
+    __syncwarp();  // reconverge the warp before the CTA barrier below (lane 0 alone ran the producer)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -266,12 +272,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc_commit(done_bar);
       mbar_wait(done_bar, 0, EX_DEVERR_WAIT_MMA);
     }
+    __syncwarp();  // reconverge the warp before the CTA barrier below (lane 0 alone issued the MMAs)
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..5)
     const int q = warp & 3;            // TMEM lane quarter this warp may access
     const int row = 32 * q + lane;     // weight row inside the tile = TMEM lane
     const int et = threadIdx.x - 64;   // 0..127
     const uint32_t lane_off = (uint32_t)(32 * q) << 16;
+    long long* my_stage = stage_red + (size_t)(warp - 2) * 2 * TC_RED_TOK * 32;  // this warp's two buffers
+    uint32_t nbulk = 0;  // bulk reduce-adds issued by this warp (selects and recycles the staging buffers)
     TcWalk walk(a);
     TcSeg sg;
     int seg_i = 0;
@@ -285,8 +294,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int n = n_tile * 128 + row;
       const int m0 = m_tile * BT;
       const bool whole = (sg.kb == 0 && sg.ke == a.KI);
+      // A split tile owns workspace slot b* = the first CTA boundary strictly inside it; every contributor computes
+      // the same b*, distinct split tiles get distinct slots, and b* < G. Slot layout: [lane quarter][token][32 rows].
+      const int slot = whole ? 0 : (int)((((int64_t)sg.tile * a.KI + 1) * a.G + a.T - 1) / a.T);
+      long long* slot_q = a.ws_acc + ((int64_t)slot * 4 + q) * BT * 32;
       const uint32_t t_hh = tmem_base + lane_off + (uint32_t)(buf * cb);
-constexpr int CW = BT < 16 ? 8 : 16;  // TMEM columns read per tcgen05.ld
+      constexpr int CW = BT < 16 ? 8 : 16;  // TMEM columns read per tcgen05.ld
 #pragma unroll 1
       for (int c = 0; c < BT; c += CW) {
         uint32_t vh[CW], vm[CW], vl[CW];
@@ -298,31 +311,51 @@ constexpr int CW = BT < 16 ? 8 : 16;  // TMEM columns read per tcgen05.ld
           tc_fence_before();
           mbar_arrive(tempty_bar + buf);
         }
-        if (n < a.N) {
+        if (whole) {
+          if (n < a.N) {
 #pragma unroll
-          for (int j = 0; j < CW; ++j) {
-            const int t = m0 + c + j;
-            if (t < a.M) {
-              const long long tot = ex_combine((int)vh[j], (int)vm[j], a.trunc ? 0 : (int)vl[j]);
-              if (whole)
-                tc_finish(tot, t, n, a);
-              else
-                red_add_s64(a.ws_acc + (int64_t)t * a.N + n, tot);
+            for (int j = 0; j < CW; ++j) {
+              const int t = m0 + c + j;
+              if (t < a.M) tc_finish(ex_combine((int)vh[j], (int)vm[j], a.trunc ? 0 : (int)vl[j]), t, n, a);
             }
+          }
+        } else {
+          // stage 8 tokens x 32 rows in shared memory, then one 2 KB bulk reduce-add into the slot (TMA engine)
+#pragma unroll
+          for (int j0 = 0; j0 < CW; j0 += TC_RED_TOK) {
+            long long* sb = my_stage + (size_t)(nbulk & 1) * TC_RED_TOK * 32;
+            if (nbulk >= 2 && lane == 0) bulk_wait_read<1>();  // the reduce that last read this buffer is done
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < TC_RED_TOK; ++j)
+              sb[j * 32 + lane] = ex_combine((int)vh[j0 + j], (int)vm[j0 + j], a.trunc ? 0 : (int)vl[j0 + j]);
+            fence_proxy_async_shared();  // make the generic-proxy writes visible to the bulk copy
+            __syncwarp();
+            if (lane == 0) {
+              bulk_reduce_add_u64(slot_q + (int64_t)(c + j0) * 32, sb, TC_RED_TOK * 32 * 8);
+              bulk_commit();
+            }
+            ++nbulk;
           }
         }
       }
       ++seg_i;
       if (whole) continue;
-      // split tile: ticket on k-iterations; the CTA that completes the tile finishes it
+      // split tile: wait until this warp's reduce-adds are performed, then take a ticket counting k-iterations;
+      // the CTA that completes the tile finishes it
+      if (lane == 0) {
+        bulk_wait_all();
+        fence_proxy_async_global();
+      }
+      __syncwarp();
       __threadfence();
       mbar_arrive(epi_bar);
       if (et == 0) {
         int flag = 0;
         if (mbar_wait(epi_bar, epi_phase, EX_DEVERR_WAIT_MMA)) {
-          const int old = atomicAdd(a.ws_cnt + sg.tile, sg.ke - sg.kb);
+          const int old = atomicAdd(a.ws_cnt + slot, sg.ke - sg.kb);
           flag = (old + (sg.ke - sg.kb) == a.KI) ? 1 : 0;
-          if (flag) a.ws_cnt[sg.tile] = 0;
+          if (flag) a.ws_cnt[slot] = 0;
         }
         *(volatile int*)last_flag = flag;
         mbar_arrive(flag_bar);
@@ -330,18 +363,31 @@ constexpr int CW = BT < 16 ? 8 : 16;  // TMEM columns read per tcgen05.ld
       if (!mbar_wait(flag_bar, epi_phase, EX_DEVERR_WAIT_MMA)) break;
       epi_phase ^= 1;
       if (*(volatile int*)last_flag) {
+        // This CTA completed the tile: every contribution is in L2. Read the slot back in batches of independent
+        // L2 loads, finish, and zero it for the next call.
         __threadfence();
         if (n < a.N) {
           const int tmax = min(BT, a.M - m0);
-          for (int j = 0; j < tmax; ++j) {
-            const int t = m0 + j;
-            const long long tot = (long long)atomicExch(
-                reinterpret_cast<unsigned long long*>(a.ws_acc + (int64_t)t * a.N + n), 0ull);
-            tc_finish(tot, t, n, a);
+          long long* sp = slot_q + lane;
+          constexpr int CH = BT < 16 ? BT : 16;
+#pragma unroll 1
+          for (int j0 = 0; j0 < tmax; j0 += CH) {
+            long long v[CH];
+#pragma unroll
+            for (int j = 0; j < CH; ++j) v[j] = (j0 + j < tmax) ? __ldcg(sp + (int64_t)(j0 + j) * 32) : 0ll;
+#pragma unroll
+            for (int j = 0; j < CH; ++j) {
+              if (j0 + j < tmax) {
+                __stcg(sp + (int64_t)(j0 + j) * 32, 0ll);
+                tc_finish(v[j], m0 + j0 + j, n, a);
+              }
+            }
           }
         }
       }
     }
+    if (lane == 0) bulk_wait_all();  // no bulk copy may still read shared memory when the CTA exits
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -422,12 +468,13 @@ static TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int split_k, int algo, in
   G = std::min<int64_t>(G, 2147483647);
   p.G = (int)G;
   const size_t stage = tc_stage_bytes(p.BT);
-  const size_t overhead = 1024 + 256;  // alignment slack + barriers
+  const size_t overhead = 1024 + 256 + TC_RED_STAGING;  // alignment slack + barriers + reduce staging
   p.stages = (int)std::min<size_t>(8, (TC_SMEM_BUDGET - overhead) / stage);
   p.smem = (size_t)p.stages * stage + overhead;
   const bool aligned = (G <= tiles) && (tiles % G == 0);
-  p.cnt_bytes = (size_t)((tiles * 4 + 255) / 256 * 256);
-  p.ws_bytes = aligned ? 0 : p.cnt_bytes + (size_t)M * N * 8;
+  p.cnt_bytes = (size_t)((G * 4 + 255) / 256 * 256);
+  p.ws_bytes = aligned ? 0 : p.cnt_bytes + (size_t)G * p.BT * 128 * 8;  // one int64 tile slot per CTA boundary
+  // (slot layout [4 lane quarters][BT tokens][32 rows]: each epilogue warp reduces contiguous 2 KB pieces)
   return p;
 }
 

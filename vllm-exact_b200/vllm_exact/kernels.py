@@ -49,10 +49,10 @@ _WS = {}
 _WS_LOCK = threading.Lock()
 
 
-def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor | None:
+def _workspace(dev: torch.device, nbytes: int, stream: int | None = None) -> torch.Tensor | None:
     if nbytes <= 0:
         return None
-    key = (dev.index, _stream(dev))
+    key = (dev.index, _stream(dev) if stream is None else stream)
     with _WS_LOCK:
         ws = _WS.get(key)
         if ws is None or ws.numel() < nbytes:
@@ -62,10 +62,11 @@ def _workspace(dev: torch.device, nbytes: int) -> torch.Tensor | None:
     return ws
 
 
-def reserve_workspace(nbytes: int, device=None) -> None:
-    """Pre-allocate the split-K workspace of the current stream (call before CUDA-graph capture)."""
+def reserve_workspace(nbytes: int, device=None, stream=None) -> None:
+    """Pre-allocate the split-K workspace of `stream` (default: the current stream), e.g. for the stream a CUDA graph
+    will be captured on: a workspace first allocated during capture is zero-filled on every replay."""
     dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device(device).index)
-    _workspace(dev, nbytes)
+    _workspace(dev, nbytes, None if stream is None else stream.cuda_stream)
 
 
 # ------------------------------------------------------------------------------------------------------------------
