@@ -108,6 +108,27 @@ int ex_linear(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* cx
               size_t workspace_bytes, int split_k, int algo, void* stream);
 
 /*
+ * ex_linear for callers that cannot allocate device memory: same arguments and results as ex_linear, minus the
+ * workspace. No counterpart in the reference (its split-K path allocates a fresh int64 workspace with torch.empty on
+ * every call, kernels.py:273). Some callers cannot do that, or call cudaMalloc themselves: a serving engine that has
+ * already reserved nearly all device memory for its KV cache (an extra allocation fails or fragments its pool), a
+ * plugin host that owns every device allocation, or code running inside a region where allocation calls are not
+ * allowed. This entry point allocates nothing: its split-K scratch is a static device array of
+ * EX_NOALLOC_SCRATCH_BYTES inside this library, which every GPU that loads the library holds until the process exits.
+ *   - The first call on a device looks up the array's device address and clears it on `stream`; make that first
+ *     call before any stream capture.
+ *   - Shapes whose split-K plan needs more scratch than EX_NOALLOC_SCRATCH_BYTES are rejected with EX_ERR_WORKSPACE
+ *     (ex_last_error_string() says so) before anything is launched.
+ *   - All calls share the one array and leave it zeroed; calls that overlap on the GPU (two streams, or two
+ *     threads) race on it and must be serialized by the caller.
+ */
+#define EX_NOALLOC_SCRATCH_BYTES (24u << 20)
+int ex_linear_noalloc(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* cx, const int32_t* sx,
+                      const int8_t* wh, const int8_t* wl, int64_t ldw, const int32_t* cw, const int32_t* sw,
+                      int64_t M, int64_t N, int64_t K, int F, int trunc, void* out, int out_dtype, int64_t ldo,
+                      int split_k, int algo, void* stream);
+
+/*
  * Integer part of ex_linear without the scaling epilogue: tot (M x N int64, ld ldt) = the exact integer total
  * of this K slice, including the F == 15 offset terms of the slice. Summing the tot of disjoint K slices (e.g. an
  * int64 all-reduce over K-sharded ranks) gives exactly the tot of the whole K range. This is the row-parallel

@@ -3,6 +3,7 @@
 // The whole library is one translation unit (this file includes the kernel headers) so that every kernel shares the
 // single device error word g_ex_dev_error. Every entry point validates its arguments before launching anything,
 // never allocates device memory and never synchronizes the host.
+#include <mutex>
 #include <string>
 
 #include "ex_common.cuh"
@@ -10,6 +11,11 @@
 #include "ex_gemm_simt.cuh"
 #include "ex_gemm_tc.cuh"
 #include "ex_paged_decode.cuh"
+
+// Split-K scratch of ex_linear_noalloc: a file-scope device array, so that entry point never allocates. Host code
+// must not hand this symbol to a kernel (on the host it is only a stand-in); the device address is looked up once per
+// device with cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_ex_noalloc_scratch[EX_NOALLOC_SCRATCH_BYTES];
 
 namespace {
 
@@ -157,6 +163,28 @@ int linear_impl(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* 
   return EX_ERR_ARG;
 }
 
+// Per-device address of g_ex_noalloc_scratch, looked up (and the array cleared) on the first call on each device.
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[128] = {};
+
+int noalloc_scratch(cudaStream_t st, void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_status(e);
+  if (dev < 0 || dev >= 128) return EX_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_ex_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_status(e);
+    e = cudaMemsetAsync(p, 0, EX_NOALLOC_SCRATCH_BYTES, st);  // split-K slots and tickets must start at zero
+    if (e != cudaSuccess) return cuda_status(e);
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return EX_OK;
+}
+
 size_t linear_ws(int64_t M, int64_t N, int64_t K, int split_k, int algo) {
   if (M <= 0 || N <= 0) return 0;
   if (algo == EX_ALGO_AUTO) algo = EX_ALGO_TC_I8;  // TC plans need at least as much as SIMT ones, sized generously
@@ -245,6 +273,32 @@ int ex_linear(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* cx
               size_t workspace_bytes, int split_k, int algo, void* stream) {
   return linear_impl<false>(xh, xl, ldx, cx, sx, wh, wl, ldw, cw, sw, M, N, K, F, trunc, out, out_dtype, ldo,
                             workspace, workspace_bytes, split_k, algo, (cudaStream_t)stream);
+}
+
+int ex_linear_noalloc(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* cx, const int32_t* sx,
+                      const int8_t* wh, const int8_t* wl, int64_t ldw, const int32_t* cw, const int32_t* sw,
+                      int64_t M, int64_t N, int64_t K, int F, int trunc, void* out, int out_dtype, int64_t ldo,
+                      int split_k, int algo, void* stream) {
+  int rc = check_linear_args(xh, xl, ldx, cx, wh, wl, ldw, cw, M, N, K, F, out, ldo);
+  if (rc != EX_OK || M == 0 || N == 0) return rc;
+  if (split_k < 0) return EX_ERR_ARG;
+  const int chosen = pick_algo(algo, xh, xl, ldx, wh, wl, ldw, M, N, K);
+  size_t need = 0;
+  if (chosen == EX_ALGO_SIMT)
+    need = simt_plan(M, N, K, split_k).ws_bytes;
+  else if (chosen == EX_ALGO_TC_I8 && ex::tc_supported(xh, xl, ldx, wh, wl, ldw, M, N, K))
+    need = ex::tc_plan(M, N, K, split_k, chosen, num_sms()).ws_bytes;
+  if (need > EX_NOALLOC_SCRATCH_BYTES) {
+    g_last_error = "ex_linear_noalloc: this shape's split-K plan needs " + std::to_string(need) +
+                   " bytes of scratch, more than the static EX_NOALLOC_SCRATCH_BYTES (" +
+                   std::to_string((size_t)EX_NOALLOC_SCRATCH_BYTES) + ")";
+    return EX_ERR_WORKSPACE;
+  }
+  void* scratch = nullptr;
+  rc = noalloc_scratch((cudaStream_t)stream, &scratch);
+  if (rc != EX_OK) return rc;
+  return linear_impl<false>(xh, xl, ldx, cx, sx, wh, wl, ldw, cw, sw, M, N, K, F, trunc, out, out_dtype, ldo, scratch,
+                            EX_NOALLOC_SCRATCH_BYTES, split_k, algo, (cudaStream_t)stream);
 }
 
 int ex_linear_partial_i64(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* cx, const int8_t* wh,

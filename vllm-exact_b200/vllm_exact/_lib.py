@@ -28,6 +28,8 @@ SIGNATURES = {
     "ex_linear_workspace_bytes": (c_sz, [c_i64, c_i64, c_i64, c_i32, c_i32]),
     "ex_linear": (c_i32, [c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i32,
                           c_i32, c_vp, c_i32, c_i64, c_vp, c_sz, c_i32, c_i32, c_vp]),
+    "ex_linear_noalloc": (c_i32, [c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64,
+                                  c_i32, c_i32, c_vp, c_i32, c_i64, c_i32, c_i32, c_vp]),
     "ex_linear_partial_i64": (c_i32, [c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i32,
                                       c_i32, c_vp, c_i64, c_vp, c_sz, c_i32, c_i32, c_vp]),
     "ex_epilogue_i64": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_i64, c_vp]),
