@@ -373,9 +373,9 @@ int ex_paged_decode(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cac
     const int smem = ex::PdCfg<DD>::SMEM;                                                                        \
     e = cudaFuncSetAttribute(ex::k_paged_partial<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);        \
     if (e == cudaSuccess)                                                                                        \
-      ex::k_paged_partial<DD><<<grid, ex::PD_THREADS, smem, st>>>(qp, sq_t, sq_h, kp, vp, s_block, s_page,       \
-                                                                   s_head, block_table, sbt, seq_lens, H, G, BS, \
-                                                                   scale, split, NS, ws_m, ws_l, ws_acc);        \
+      e = ex_launch_pdl(ex::k_paged_partial<DD>, grid, dim3(ex::PD_THREADS), smem, st, qp, sq_t, sq_h, kp, vp,   \
+                        s_block, s_page, s_head, block_table, sbt, seq_lens, H, G, BS, scale, split, NS, ws_m,   \
+                        ws_l, ws_acc);                                                                           \
   }
   if (D == 64) EX_PD_LAUNCH(64)
   else if (D == 128) EX_PD_LAUNCH(128)
@@ -384,12 +384,14 @@ int ex_paged_decode(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cac
   if (e != cudaSuccess) return cuda_status(e);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e);
   const int mthreads = std::min(D, 256);
+  const dim3 mg(n * H), mb(mthreads);
   if (out_dtype == EX_DTYPE_BF16)
-    ex::k_paged_merge<EX_DTYPE_BF16><<<n * H, mthreads, 0, st>>>(ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
+    e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_BF16>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
   else if (out_dtype == EX_DTYPE_F16)
-    ex::k_paged_merge<EX_DTYPE_F16><<<n * H, mthreads, 0, st>>>(ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
+    e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_F16>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
   else
-    ex::k_paged_merge<EX_DTYPE_F32><<<n * H, mthreads, 0, st>>>(ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
+    e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_F32>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
+  if (e != cudaSuccess) return cuda_status(e);
   return cuda_status(cudaGetLastError());
 }
 

@@ -11,6 +11,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "vllm_exact_b200.h"
 
 #define EX_WAIT_TIMEOUT_NS 2000000000ull  // 2 s: far above any legitimate in-kernel wait
@@ -134,6 +136,21 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Prefetch a tile into L2 only (no shared-memory write). L2 is coherent with every writer, so this is safe even
+// before griddepcontrol.wait.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+
+// Programmatic dependent launch: wait until the preceding kernel in the stream has completed and its memory is
+// visible (no-op when launched without the attribute), and allow the next kernel to begin launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -245,6 +262,26 @@ __device__ __forceinline__ uint32_t elect_one() {
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(pred));
   return pred;
+}
+
+// ------------------------------------------------------------------------------------------------------------------
+// Launch with the programmatic-stream-serialization attribute: the kernel may start while the previous kernel in the
+// stream is finishing; it must call pdl_wait() before touching memory that kernel produces or consumes.
+// ------------------------------------------------------------------------------------------------------------------
+template <typename... KArgs, typename... Args>
+static cudaError_t ex_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                 Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ------------------------------------------------------------------------------------------------------------------

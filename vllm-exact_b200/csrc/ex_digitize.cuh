@@ -102,6 +102,10 @@ __global__ void __launch_bounds__(DIG_THREADS) k_digitize(const T* __restrict__ 
                                                           float* __restrict__ amax_io) {
   __shared__ float redf[DIG_THREADS / 32];
   __shared__ int redi[DIG_THREADS / 32];
+  // Let the consumer (the exact GEMM) start its prologue now: everything a kernel of this library does before its
+  // own pdl_wait() is safe to overlap with this kernel. Then wait: the input comes from the previous kernel.
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t row = blockIdx.x;
   const T* xr = x + row * ldx;
   float amax = 0.0f;
@@ -174,10 +178,10 @@ static cudaError_t launch_digitize_t(const void* x, int64_t ldx, int64_t rows, i
                                            (reinterpret_cast<uintptr_t>(l) % 8 == 0)));
   dim3 grid((unsigned)rows);
   if (vec)
-    k_digitize<T, F, true, MODE><<<grid, DIG_THREADS, 0, st>>>(xp, ldx, (int)K, h, l, ldd, cs, sh, amax_io);
-  else
-    k_digitize<T, F, false, MODE><<<grid, DIG_THREADS, 0, st>>>(xp, ldx, (int)K, h, l, ldd, cs, sh, amax_io);
-  return cudaGetLastError();
+    return ex_launch_pdl(k_digitize<T, F, true, MODE>, grid, dim3(DIG_THREADS), 0, st, xp, ldx, (int)K, h, l, ldd, cs,
+                         sh, amax_io);
+  return ex_launch_pdl(k_digitize<T, F, false, MODE>, grid, dim3(DIG_THREADS), 0, st, xp, ldx, (int)K, h, l, ldd, cs,
+                       sh, amax_io);
 }
 
 template <typename T, int MODE>

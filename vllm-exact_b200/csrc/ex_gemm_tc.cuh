@@ -178,6 +178,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // Programmatic dependent launch: this prologue may overlap the previous kernel (typically the activation
+  // digitizer). Before waiting, only warm L2 with this CTA's first weight tiles (L2 is coherent with any writer, so
+  // this is safe even if the previous kernel wrote them); every shared-memory load, every read of activations or
+  // scales and every write happens after pdl_wait().
+  if (warp == 0 && lane == 0) {
+    TcWalk walk(a);
+    TcSeg sg;
+    int left = S;
+    while (left > 0 && walk.next(sg)) {
+      const int n_tile = sg.tile / a.m_tiles;
+      for (int kt = sg.kb; kt < sg.ke && left > 0; ++kt, --left) {
+        tma_prefetch_l2_2d(&tm_wh, kt * TC_BK, n_tile * 128);
+        tma_prefetch_l2_2d(&tm_wl, kt * TC_BK, n_tile * 128);
+      }
+    }
+  }
+  pdl_launch_dependents();
+  pdl_wait();
+
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -497,8 +516,7 @@ static cudaError_t launch_tc_bt(const TcPlan& p, const TcArgs& a, const CUtensor
                                 const CUtensorMap& mxh, const CUtensorMap& mxl, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(k_exact_tc_i8<BT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
   if (e != cudaSuccess) return e;
-  k_exact_tc_i8<BT><<<p.G, TC_THREADS, p.smem, st>>>(mwh, mwl, mxh, mxl, a);
-  return cudaGetLastError();
+  return ex_launch_pdl(k_exact_tc_i8<BT>, dim3(p.G), dim3(TC_THREADS), p.smem, st, mwh, mwl, mxh, mxl, a);
 }
 
 template <bool PARTIAL>

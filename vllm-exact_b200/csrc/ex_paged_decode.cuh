@@ -81,6 +81,8 @@ __global__ void __launch_bounds__(PD_THREADS, 2)
                     float* __restrict__ ws_m, float* __restrict__ ws_l, float* __restrict__ ws_acc) {
   using C = PdCfg<D>;
   extern __shared__ __align__(1024) uint8_t pd_smem[];
+  pdl_launch_dependents();  // the merge kernel's prologue may start; it waits for this grid before reading
+  pdl_wait();               // query / cache / block table come from earlier kernels
   const int b = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int kg = warp / C::DSPLIT, dh = warp % C::DSPLIT;
@@ -308,6 +310,8 @@ template <int OUT_DTYPE>
 __global__ void k_paged_merge(const float* __restrict__ ws_m, const float* __restrict__ ws_l,
                               const float* __restrict__ ws_acc, void* out, int64_t so_t, int64_t so_h, int H, int NS,
                               int D) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int bh = blockIdx.x;
   const int b = bh / H, h = bh % H;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
