@@ -157,12 +157,14 @@ size_t ex_paged_decode_workspace_bytes(int n, int H, int D, int max_len, int spl
  * fixed segments of `split` keys (NS = ceil(max_len / split) segments) merged in fixed order, so a request's output
  * bits do not depend on n, on the other requests, or on where its pages are placed.
  *   q        (>= n) x H x D, strides (sq_t, sq_h, 1), bf16
- *   k_cache, v_cache: num_blocks x BS x KV x D with strides (s_block, s_page, s_head, 1), bf16
+ *   k_cache, v_cache: num_blocks x BS x KV x D with strides (s_block, s_page, s_head, 1), bf16; block-table entries
+ *            must lie in [0, num_blocks) for every token below seq_lens
  *   block_table int32 (n x pages, row stride sbt); seq_lens int32 (n)
  *   out      (>= n) x H x D, strides (so_t, so_h, 1), out_dtype (bf16, fp16 or fp32)
  */
 int ex_paged_decode(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cache, const void* v_cache,
-                    int64_t s_block, int64_t s_page, int64_t s_head, const int32_t* block_table, int64_t sbt,
+                    int64_t s_block, int64_t s_page, int64_t s_head, int64_t num_blocks, const int32_t* block_table,
+                    int64_t sbt,
                     const int32_t* seq_lens, int n, int H, int KV, int D, int BS, float scale, int max_len, int split,
                     void* out, int64_t so_t, int64_t so_h, int out_dtype, void* workspace, size_t workspace_bytes,
                     void* stream);

@@ -62,8 +62,8 @@ def test_argument_validation_without_gpu(L):
     assert L.ex_linear_workspace_bytes(4, 8, 4096, 1, X.EX_ALGO_SIMT) == 0
     # epilogue / paged decode
     assert L.ex_epilogue_i64(p, 4, p, p, 4, 8, p, 1, 8, None) == X.EX_ERR_ARG
-    pd = lambda H, KV, D, ws, wsb: (p, 64, 32, ctypes.c_void_p(256), ctypes.c_void_p(256), 64, 64, 64, p, 4, p, 2, H,
-                                   KV, D, 16, 0.1, 4096, 4096, p, 64, 32, 1, ws, wsb, None)
+    pd = lambda H, KV, D, ws, wsb: (p, 64, 32, ctypes.c_void_p(256), ctypes.c_void_p(256), 64, 64, 64, 100, p, 4, p,
+                                   2, H, KV, D, 16, 0.1, 4096, 4096, p, 64, 32, 1, ws, wsb, None)
     assert L.ex_paged_decode(*pd(32, 6, 128, None, 0)) == X.EX_ERR_ARG      # H % KV != 0
     assert L.ex_paged_decode(*pd(32, 8, 96, None, 0)) == X.EX_ERR_UNSUPPORTED  # head size
     assert L.ex_paged_decode(*pd(64, 2, 128, None, 0)) == X.EX_ERR_UNSUPPORTED  # 32 query heads per KV head

@@ -11,6 +11,7 @@
 #include "ex_gemm_simt.cuh"
 #include "ex_gemm_tc.cuh"
 #include "ex_paged_decode.cuh"
+#include "ex_paged_decode_tma.cuh"
 
 // Split-K scratch of ex_linear_noalloc: a file-scope device array, so that entry point never allocates. Host code
 // must not hand this symbol to a kernel (on the host it is only a stand-in); the device address is looked up once per
@@ -185,6 +186,35 @@ int noalloc_scratch(cudaStream_t st, void** out) {
   return EX_OK;
 }
 
+// 4-D tensor map over a paged K or V cache: (head dim, KV head, offset in page, page), 16-token x 64-dim boxes.
+bool encode_kv_map(CUtensorMap* map, const void* base, int D, int KV, int BS, int64_t num_blocks, int64_t s_head,
+                   int64_t s_page, int64_t s_block) {
+  ex::PFN_encodeTiled enc = ex::get_encode_fn();
+  if (!enc || reinterpret_cast<uintptr_t>(base) % 16 != 0) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)KV, (cuuint64_t)BS, (cuuint64_t)num_blocks};
+  cuuint64_t strides[3] = {(cuuint64_t)s_head * 2, (cuuint64_t)s_page * 2, (cuuint64_t)s_block * 2};
+  cuuint32_t box[4] = {64, 1, 16, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int launch_merge(const float* ws_m, const float* ws_l, const float* ws_acc, void* out, int64_t so_t, int64_t so_h,
+                 int n, int H, int NS, int D, int out_dtype, cudaStream_t st) {
+  const int mthreads = std::min(D, 256);
+  const dim3 mg(n * H), mb(mthreads);
+  cudaError_t e;
+  if (out_dtype == EX_DTYPE_BF16)
+    e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_BF16>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
+  else if (out_dtype == EX_DTYPE_F16)
+    e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_F16>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
+  else
+    e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_F32>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
+  if (e != cudaSuccess) return cuda_status(e);
+  return cuda_status(cudaGetLastError());
+}
+
 size_t linear_ws(int64_t M, int64_t N, int64_t K, int split_k, int algo) {
   if (M <= 0 || N <= 0) return 0;
   if (algo == EX_ALGO_AUTO) algo = EX_ALGO_TC_I8;  // TC plans need at least as much as SIMT ones, sized generously
@@ -337,7 +367,8 @@ size_t ex_paged_decode_workspace_bytes(int n, int H, int D, int max_len, int spl
 }
 
 int ex_paged_decode(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cache, const void* v_cache,
-                    int64_t s_block, int64_t s_page, int64_t s_head, const int32_t* block_table, int64_t sbt,
+                    int64_t s_block, int64_t s_page, int64_t s_head, int64_t num_blocks, const int32_t* block_table,
+                    int64_t sbt,
                     const int32_t* seq_lens, int n, int H, int KV, int D, int BS, float scale, int max_len, int split,
                     void* out, int64_t so_t, int64_t so_h, int out_dtype, void* workspace, size_t workspace_bytes,
                     void* stream) {
@@ -368,6 +399,28 @@ int ex_paged_decode(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cac
   const __nv_bfloat16* vp = reinterpret_cast<const __nv_bfloat16*>(v_cache);
   dim3 grid(n, KV, NS);
   cudaError_t e = cudaSuccess;
+  if (num_blocks <= 0) return EX_ERR_ARG;
+  // TMA page-gather kernel for the common layouts; the cp.async kernel below handles everything else
+  if ((D == 64 || D == 128) && G <= 8 && BS % 16 == 0 && split % ex::PT_BLK == 0 && ex::device_is_sm100()) {
+    CUtensorMap mk, mv;
+    if (encode_kv_map(&mk, k_cache, D, KV, BS, num_blocks, s_head, s_page, s_block) &&
+        encode_kv_map(&mv, v_cache, D, KV, BS, num_blocks, s_head, s_page, s_block)) {
+      const dim3 blk(ex::PT_THREADS);
+#define EX_PT_LAUNCH(DD)                                                                                         \
+  {                                                                                                              \
+    const int smem = ex::PtCfg<DD>::SMEM;                                                                        \
+    e = cudaFuncSetAttribute(ex::k_paged_tma<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);            \
+    if (e == cudaSuccess)                                                                                        \
+      e = ex_launch_pdl(ex::k_paged_tma<DD>, grid, blk, smem, st, mk, mv, qp, sq_t, sq_h, block_table, sbt,      \
+                        seq_lens, H, G, BS, scale, split, NS, ws_m, ws_l, ws_acc);                               \
+  }
+      if (D == 64) EX_PT_LAUNCH(64)
+      else EX_PT_LAUNCH(128)
+#undef EX_PT_LAUNCH
+      if (e != cudaSuccess) return cuda_status(e);
+      return launch_merge(ws_m, ws_l, ws_acc, out, so_t, so_h, n, H, NS, D, out_dtype, st);
+    }
+  }
 #define EX_PD_LAUNCH(DD)                                                                                         \
   {                                                                                                              \
     const int smem = ex::PdCfg<DD>::SMEM;                                                                        \
@@ -383,16 +436,7 @@ int ex_paged_decode(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cac
 #undef EX_PD_LAUNCH
   if (e != cudaSuccess) return cuda_status(e);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e);
-  const int mthreads = std::min(D, 256);
-  const dim3 mg(n * H), mb(mthreads);
-  if (out_dtype == EX_DTYPE_BF16)
-    e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_BF16>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
-  else if (out_dtype == EX_DTYPE_F16)
-    e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_F16>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
-  else
-    e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_F32>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
-  if (e != cudaSuccess) return cuda_status(e);
-  return cuda_status(cudaGetLastError());
+  return launch_merge(ws_m, ws_l, ws_acc, out, so_t, so_h, n, H, NS, D, out_dtype, st);
 }
 
 }  // extern "C"

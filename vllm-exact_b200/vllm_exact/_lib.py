@@ -34,8 +34,8 @@ SIGNATURES = {
                                       c_i32, c_vp, c_i64, c_vp, c_sz, c_i32, c_i32, c_vp]),
     "ex_epilogue_i64": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_i64, c_vp]),
     "ex_paged_decode_workspace_bytes": (c_sz, [c_i32, c_i32, c_i32, c_i32, c_i32]),
-    "ex_paged_decode": (c_i32, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_i32, c_i32,
-                                c_i32, c_i32, c_i32, c_f32, c_i32, c_i32, c_vp, c_i64, c_i64, c_i32, c_vp, c_sz,
+    "ex_paged_decode": (c_i32, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_i32,
+                                c_i32, c_i32, c_i32, c_i32, c_f32, c_i32, c_i32, c_vp, c_i64, c_i64, c_i32, c_vp, c_sz,
                                 c_vp]),
 }
 

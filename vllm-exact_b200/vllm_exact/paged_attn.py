@@ -61,7 +61,7 @@ def paged_decode(query, key_cache, value_cache, block_table, seq_lens, scale, ou
     with torch.cuda.device(query.device):
         check("ex_paged_decode", lib().ex_paged_decode(
             query.data_ptr(), query.stride(0), query.stride(1), key_cache.data_ptr(), value_cache.data_ptr(),
-            key_cache.stride(0), key_cache.stride(1), key_cache.stride(2), block_table.data_ptr(),
+            key_cache.stride(0), key_cache.stride(1), key_cache.stride(2), key_cache.shape[0], block_table.data_ptr(),
             block_table.stride(0), seq_lens.data_ptr(), n, H, KV, D, BS, float(scale), MAX_LEN, split,
             out.data_ptr(), out.stride(0), out.stride(1), _DT[out.dtype], workspace.data_ptr(), nbytes,
             torch.cuda.current_stream(query.device).cuda_stream))
