@@ -31,13 +31,15 @@
 namespace ex {
 
 constexpr int64_t EX_MAX_K = 65536;  // int32 accumulators: |md| <= 2^15 K must stay below 2^31
-constexpr int TC_THREADS = 192;
+constexpr int TC_EPI_WARPS = 8;  // two epilogue warps per TMEM lane quarter, splitting the token chunks
+constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;
 constexpr int TC_BK = 128;               // K bytes (int8 elements) per pipeline stage = one 128-byte swizzle row
 constexpr int TC_WTILE = 128 * TC_BK;    // bytes of one weight digit tile
 constexpr int TC_SMEM_BUDGET = 220 * 1024;
 constexpr int TC_TMEM_COLS = 512;
-constexpr int TC_RED_TOK = 8;                                // tokens per bulk reduce-add (2 KB per warp)
-constexpr int TC_RED_STAGING = 4 * 2 * TC_RED_TOK * 32 * 8;  // 4 warps x 2 buffers x 8 tokens x 32 rows x int64
+constexpr int TC_RED_TOK = 4;  // tokens per bulk reduce-add (1 KB per warp)
+constexpr int TC_RED_STAGING = TC_EPI_WARPS * 2 * TC_RED_TOK * 32 * 8;  // per warp 2 buffers x 4 tokens x 32 rows x int64
+constexpr int TC_TOK_WORDS = TC_EPI_WARPS * 2 * 128 * 4;                // per warp (sx, cx) x up to 128 tokens x int32
 
 struct TcPlan {
   int BT;        // token tile
@@ -90,20 +92,56 @@ struct TcWalk {
   }
 };
 
-__device__ __forceinline__ void tc_finish(long long tot, int t, int n, const TcArgs& a) {
-  if (a.F == 15) tot += 128ll * ((long long)a.cx[t] + (long long)a.cw[n]) + 16384ll * (long long)a.K;
-  const int64_t idx = (int64_t)t * a.ldo + n;
+// Epilogue of CW consecutive tokens m0+j (j < CW, t < M) of weight row n: F = 15 offset correction over the call's K,
+// then the raw int64 total (partial mode) or the scaled, rounded output. The per-row and per-token scale words are
+// loaded once, up front, through the read-only path (interleaving them with the output stores would serialise a
+// memory round trip per element).
+// sxs / cxs: this tile's per-token scale words, already in shared memory; swn / cwn: this weight row's.
+template <int CW>
+__device__ __forceinline__ void tc_finish_chunk(const long long (&tot)[CW], int m0, int n, const int* sxs,
+                                                const int* cxs, int swn, long long cwn, const TcArgs& a) {
+  if (n >= a.N) return;
+  const long long kc = 16384ll * (long long)a.K;
+  const int jmax = min(CW, a.M - m0);
   if (a.partial) {
-    reinterpret_cast<long long*>(a.out)[idx] = tot;
+    long long* op = reinterpret_cast<long long*>(a.out) + (int64_t)m0 * a.ldo + n;
+#pragma unroll
+    for (int j = 0; j < CW; ++j) {
+      if (j >= jmax) break;
+      long long v = tot[j];
+      if (a.F == 15) v += 128ll * ((long long)cxs[j] + cwn) + kc;
+      op[(int64_t)j * a.ldo] = v;
+    }
     return;
   }
-  const float y = ex_scale_to_f32(tot, a.sx[t], a.sw[n]);
-  if (a.out_dtype == EX_DTYPE_BF16)
-    reinterpret_cast<__nv_bfloat16*>(a.out)[idx] = __float2bfloat16_rn(y);
-  else if (a.out_dtype == EX_DTYPE_F32)
-    reinterpret_cast<float*>(a.out)[idx] = y;
-  else
-    reinterpret_cast<__half*>(a.out)[idx] = __float2half_rn(y);
+  if (a.out_dtype == EX_DTYPE_BF16) {
+    __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(a.out) + (int64_t)m0 * a.ldo + n;
+#pragma unroll
+    for (int j = 0; j < CW; ++j) {
+      if (j >= jmax) break;
+      long long v = tot[j];
+      if (a.F == 15) v += 128ll * ((long long)cxs[j] + cwn) + kc;
+      op[(int64_t)j * a.ldo] = __float2bfloat16_rn(ex_scale_to_f32_fast(v, sxs[j], swn));
+    }
+  } else if (a.out_dtype == EX_DTYPE_F32) {
+    float* op = reinterpret_cast<float*>(a.out) + (int64_t)m0 * a.ldo + n;
+#pragma unroll
+    for (int j = 0; j < CW; ++j) {
+      if (j >= jmax) break;
+      long long v = tot[j];
+      if (a.F == 15) v += 128ll * ((long long)cxs[j] + cwn) + kc;
+      op[(int64_t)j * a.ldo] = ex_scale_to_f32_fast(v, sxs[j], swn);
+    }
+  } else {
+    __half* op = reinterpret_cast<__half*>(a.out) + (int64_t)m0 * a.ldo + n;
+#pragma unroll
+    for (int j = 0; j < CW; ++j) {
+      if (j >= jmax) break;
+      long long v = tot[j];
+      if (a.F == 15) v += 128ll * ((long long)cxs[j] + cwn) + kc;
+      op[(int64_t)j * a.ldo] = __float2half_rn(ex_scale_to_f32_fast(v, sxs[j], swn));
+    }
+  }
 }
 
 template <int CW>
@@ -135,7 +173,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int S = a.stages;
   // per epilogue warp, two 2 KB staging buffers (8 tokens x 32 rows of int64) for bulk reduce-adds of split tiles
   long long* stage_red = reinterpret_cast<long long*>(smem + (size_t)S * Lay::STAGE);
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + (size_t)S * Lay::STAGE + TC_RED_STAGING);
+  // per epilogue warp: the current tile's per-token shifts and row sums (2 x BT int32)
+  int* tok_words = reinterpret_cast<int*>(smem + (size_t)S * Lay::STAGE + TC_RED_STAGING);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + (size_t)S * Lay::STAGE + TC_RED_STAGING + TC_TOK_WORDS);
   uint64_t* empty_bar = full_bar + S;
   uint64_t* tfull_bar = empty_bar + S;   // [2]
   uint64_t* tempty_bar = tfull_bar + 2;  // [2]
@@ -156,10 +196,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(tfull_bar + i, 1);
-      mbar_init(tempty_bar + i, 128);
+      mbar_init(tempty_bar + i, 32 * TC_EPI_WARPS);
     }
     mbar_init(done_bar, 1);
-    mbar_init(epi_bar, 128);
+    mbar_init(epi_bar, 32 * TC_EPI_WARPS);
     mbar_init(flag_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -293,12 +333,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     __syncwarp();  // reconverge the warp before the CTA barrier below (lane 0 alone issued the MMAs)
   } else {
-    // ------------------------------------------------------------------ epilogue (warps 2..5)
-    const int q = warp & 3;            // TMEM lane quarter this warp may access
-    const int row = 32 * q + lane;     // weight row inside the tile = TMEM lane
-    const int et = threadIdx.x - 64;   // 0..127
+    // ------------------------------------------------------------------ epilogue (warps 2..9)
+    // Two warps per TMEM lane quarter; warp half h takes the token chunks c with (c / CW) % 2 == h.
+    const int q = warp & 3;               // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;     // 0 or 1
+    const int row = 32 * q + lane;        // weight row inside the tile = TMEM lane
+    const int et = threadIdx.x - 64;      // 0 .. 32 * TC_EPI_WARPS - 1
     const uint32_t lane_off = (uint32_t)(32 * q) << 16;
     long long* my_stage = stage_red + (size_t)(warp - 2) * 2 * TC_RED_TOK * 32;  // this warp's two buffers
+    int* my_sx = tok_words + (warp - 2) * 2 * 128;  // this warp's copy of the tile's token shifts / row sums
+    int* my_cx = my_sx + 128;
+    constexpr int CW = BT < 32 ? 8 : 16;  // TMEM columns per tcgen05.ld (and tokens per chunk)
+    constexpr int NCH = BT / CW;          // chunks per tile; this warp takes chunks half, half + 2, ...
     uint32_t nbulk = 0;  // bulk reduce-adds issued by this warp (selects and recycles the staging buffers)
     TcWalk walk(a);
     TcSeg sg;
@@ -307,39 +353,50 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     while (walk.next(sg)) {
       const int buf = nbuf == 2 ? (seg_i & 1) : 0;
       const uint32_t use = nbuf == 2 ? (uint32_t)(seg_i >> 1) : (uint32_t)seg_i;
-      if (!mbar_wait(tfull_bar + buf, use & 1, EX_DEVERR_WAIT_MMA)) break;
-      tc_fence_after();
       const int n_tile = sg.tile / a.m_tiles, m_tile = sg.tile % a.m_tiles;
       const int n = n_tile * 128 + row;
       const int m0 = m_tile * BT;
+      // scale words of this tile, fetched while the MMAs still run (global latency is long under full HBM load)
+      __syncwarp();  // the previous segment's reads of my_sx / my_cx are done
+      for (int j = lane; j < BT; j += 32) {
+        const int t = min(m0 + j, a.M - 1);
+        my_sx[j] = a.partial ? 0 : __ldg(a.sx + t);  // partial mode has no scales (sx may be null)
+        my_cx[j] = a.F == 15 ? __ldg(a.cx + t) : 0;
+      }
+      const int swn = (a.partial || n >= a.N) ? 0 : __ldg(a.sw + n);
+      const long long cwn = (a.F == 15 && n < a.N) ? (long long)__ldg(a.cw + n) : 0ll;
+      __syncwarp();
+      if (!mbar_wait(tfull_bar + buf, use & 1, EX_DEVERR_WAIT_MMA)) break;
+      tc_fence_after();
       const bool whole = (sg.kb == 0 && sg.ke == a.KI);
       // A split tile owns workspace slot b* = the first CTA boundary strictly inside it; every contributor computes
       // the same b*, distinct split tiles get distinct slots, and b* < G. Slot layout: [lane quarter][token][32 rows].
       const int slot = whole ? 0 : (int)((((int64_t)sg.tile * a.KI + 1) * a.G + a.T - 1) / a.T);
       long long* slot_q = a.ws_acc + ((int64_t)slot * 4 + q) * BT * 32;
       const uint32_t t_hh = tmem_base + lane_off + (uint32_t)(buf * cb);
-      constexpr int CW = BT < 16 ? 8 : 16;  // TMEM columns read per tcgen05.ld
+      if (half >= NCH) {  // no chunk for this warp (BT = 8): release the accumulator right away
+        tc_fence_before();
+        mbar_arrive(tempty_bar + buf);
+      }
 #pragma unroll 1
-      for (int c = 0; c < BT; c += CW) {
+      for (int ci = half; ci < NCH; ci += 2) {
+        const int c = ci * CW;
         uint32_t vh[CW], vm[CW], vl[CW];
         tmem_ldc<CW>(t_hh + c, vh);
         tmem_ldc<CW>(t_hh + BT + c, vm);
         if (!a.trunc) tmem_ldc<CW>(t_hh + 2 * BT + c, vl);
         tmem_ld_wait();
-        if (c + CW >= BT) {  // every TMEM read of this buffer is done: hand it back to the MMA warp
+        if (ci + 2 >= NCH) {  // this warp's TMEM reads of the buffer are done: hand it back to the MMA warp
           tc_fence_before();
           mbar_arrive(tempty_bar + buf);
         }
         if (whole) {
-          if (n < a.N) {
+          long long tot[CW];
 #pragma unroll
-            for (int j = 0; j < CW; ++j) {
-              const int t = m0 + c + j;
-              if (t < a.M) tc_finish(ex_combine((int)vh[j], (int)vm[j], a.trunc ? 0 : (int)vl[j]), t, n, a);
-            }
-          }
+          for (int j = 0; j < CW; ++j) tot[j] = ex_combine((int)vh[j], (int)vm[j], a.trunc ? 0 : (int)vl[j]);
+          tc_finish_chunk<CW>(tot, m0 + c, n, my_sx + c, my_cx + c, swn, cwn, a);
         } else {
-          // stage 8 tokens x 32 rows in shared memory, then one 2 KB bulk reduce-add into the slot (TMA engine)
+          // stage 4 tokens x 32 rows in shared memory, then one 1 KB bulk reduce-add into the slot (TMA engine)
 #pragma unroll
           for (int j0 = 0; j0 < CW; j0 += TC_RED_TOK) {
             long long* sb = my_stage + (size_t)(nbulk & 1) * TC_RED_TOK * 32;
@@ -388,19 +445,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (n < a.N) {
           const int tmax = min(BT, a.M - m0);
           long long* sp = slot_q + lane;
-          constexpr int CH = BT < 16 ? BT : 16;
 #pragma unroll 1
-          for (int j0 = 0; j0 < tmax; j0 += CH) {
-            long long v[CH];
+          for (int ci = half; ci * CW < tmax; ci += 2) {
+            const int j0 = ci * CW;
+            long long v[CW];
 #pragma unroll
-            for (int j = 0; j < CH; ++j) v[j] = (j0 + j < tmax) ? __ldcg(sp + (int64_t)(j0 + j) * 32) : 0ll;
+            for (int j = 0; j < CW; ++j) v[j] = (j0 + j < tmax) ? __ldcg(sp + (int64_t)(j0 + j) * 32) : 0ll;
 #pragma unroll
-            for (int j = 0; j < CH; ++j) {
-              if (j0 + j < tmax) {
-                __stcg(sp + (int64_t)(j0 + j) * 32, 0ll);
-                tc_finish(v[j], m0 + j0 + j, n, a);
-              }
-            }
+            for (int j = 0; j < CW; ++j)
+              if (j0 + j < tmax) __stcg(sp + (int64_t)(j0 + j) * 32, 0ll);
+            tc_finish_chunk<CW>(v, m0 + j0, n, my_sx + j0, my_cx + j0, swn, cwn, a);
           }
         }
       }
@@ -487,7 +541,7 @@ static TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int split_k, int algo, in
   G = std::min<int64_t>(G, 2147483647);
   p.G = (int)G;
   const size_t stage = tc_stage_bytes(p.BT);
-  const size_t overhead = 1024 + 256 + TC_RED_STAGING;  // alignment slack + barriers + reduce staging
+  const size_t overhead = 1024 + 256 + TC_RED_STAGING + TC_TOK_WORDS;  // alignment, barriers, staging, scale words
   p.stages = (int)std::min<size_t>(8, (TC_SMEM_BUDGET - overhead) / stage);
   p.smem = (size_t)p.stages * stage + overhead;
   const bool aligned = (G <= tiles) && (tiles % G == 0);
