@@ -39,6 +39,9 @@ DECODE_M = [1, 16, 64]
 TENSOR_M = [256, 4096]
 ATTN = [(256, 1024), (64, 8192), (16, 16384)]
 METRIC = "exact-GEMM TB/s (exact_int8 linear, decode shapes M<=64 of the configs[1] sweep)"
+# DRAM bytes (read + write) per k_exact_tc_i8 launch, averaged over the 15 launches of one decode step, from the ncu
+# capture summarised in profiles/k_exact_tc_i8__decode_sweep.md (1.009 x the algorithmic bytes).
+GEMM_TRAFFIC_PER_LAUNCH = 331_666_637
 
 
 def peaks():
@@ -249,8 +252,10 @@ def run_ours(args):
                    "ms_per_step_with_timing_events": round(ms_events, 4)},
         "gpu_launches": launches["n"],
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4), "traffic": None, "peak_kind": peak_kind,
-                     "kernel": "k_exact_tc_i8 (all 15 decode GEMM launches; algorithmic bytes / summed durations)"},
+                     "frac": round(achieved / hbm, 4), "traffic": GEMM_TRAFFIC_PER_LAUNCH,
+                     "algorithmic_bytes_per_launch": step_bytes // len(order), "peak_kind": peak_kind,
+                     "kernel": "k_exact_tc_i8: algorithmic bytes of the 15 decode GEMM launches / their summed "
+                               "event-timed durations (= per-launch average); traffic = ncu average per launch"},
         "sweep_decode": per_gemm,
         "clocks": clk.summary(),
     }
@@ -442,8 +447,9 @@ def run_reference(args):
 
 
 def run_case(args):
-    """Small single-kernel workloads for ncu captures: `gemm:<shape>:<M>[:<algo>]` or `attn:<n>:<ctx>`; runs the
-    kernel --reps times eagerly (ncu flushes caches before each captured pass)."""
+    """Workloads for ncu captures, run eagerly --reps times (ncu flushes caches before each captured pass):
+    `gemm:<shape>:<M>[:<algo>]` one GEMM, `attn:<n>:<ctx>` one attention batch, `sweep` the 15 GEMMs of the headline
+    decode step."""
     import torch
     from vllm_exact import kernels as KK, paged_attn as PA
     import recipes as R
@@ -459,6 +465,15 @@ def run_case(args):
         y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
         for _ in range(args.reps):
             KK.exact_linear(xd, W, 14, True, out=y, cfg={"algo": algo})
+    elif kind == "sweep":
+        # one eager pass of the headline decode step: 15 x (digitize + exact GEMM)
+        W = {name: make_weight_digits(K, N, 1000 + i, dev) for i, (name, K, N) in enumerate(SHAPES)}
+        for _ in range(args.reps):
+            for M in DECODE_M:
+                for i, (name, K, N) in enumerate(SHAPES):
+                    y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+                    KK.exact_linear(KK.digitize(make_activation(M, K, 17 * M + i, dev), 14), W[name], 14, True,
+                                    out=y)
     elif kind == "attn":
         n, ctx = int(rest[0]), int(rest[1])
         PA.MAX_LEN = 20480
