@@ -28,6 +28,7 @@ import threading
 import time
 from pathlib import Path
 
+os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep NCCL's version banner off stdout: rank 0 prints one JSON line
 ROOT = Path(__file__).resolve().parent
 for p in (ROOT, ROOT / "vllm-exact_b200", ROOT / "tests" / "golden"):
     if str(p) not in sys.path:
@@ -259,10 +260,18 @@ def run_ours(args):
         "sweep_decode": per_gemm,
         "clocks": clk.summary(),
     }
+    e2e = e2e_bench(dev, W, order, args)  # every rank: whole-job end-to-end rate, max time over ranks
+    if world > 1:
+        tt = torch.tensor([e2e["ms_per_step"]], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e["ms_per_step"] = round(float(tt), 4)
+        e2e["value"] = round(world * step_bytes / (float(tt) * 1e-3) / 1e12, 4)
+        e2e["h2d_bytes_per_step"] *= world
+        e2e["d2h_bytes_per_step"] *= world
+    result["e2e"] = e2e
     if rank == 0:
         result["sweep_tensor"] = tensor_sweep(dev, W, bf16_burst, args.quick)
         result["attention"] = attention_bench(dev, hbm, args.quick)
-        result["e2e"] = e2e_bench(dev, W, order, args)
         if world == 1 and not args.quick:
             result["cpu_baseline"] = cpu_baseline(W)
     if world > 1:
