@@ -273,7 +273,10 @@ def run_ours(args):
         result["sweep_tensor"] = tensor_sweep(dev, W, bf16_burst, args.quick)
         result["attention"] = attention_bench(dev, hbm, args.quick)
         if world == 1 and not args.quick:
-            result["cpu_baseline"] = cpu_baseline(W)
+            del W, X, Y
+            torch.cuda.empty_cache()
+            result["decode_step"] = decode_step_bench(dev)
+            result["cpu_baseline"] = cpu_baseline()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -408,6 +411,112 @@ def e2e_bench(dev, W, order, args):
             "api": "torch.ops.exactmm.linear (pinned host in, pinned host out), CUDA graph per step"}
 
 
+# Hybrid decoder of BASELINE configs[4]: hidden 4096, 32 layers = 8 full-attention (GQA 32 q / 8 kv heads x 128) +
+# 24 Gated-DeltaNet layers, SwiGLU MLP 12288, vocab 151936. GDN projection sizes follow the reference's tuned shapes
+# (scripts/tune_table.py:12-13: in_proj_qkvz N=12288, in_proj_ba N=64, out_proj 4096x4096).
+HYBRID_ATTN_LAYERS = (3, 7, 11, 15, 19, 23, 27, 31)
+STEP_CONFIGS = [(256, 1024), (64, 8192), (16, 16384)]
+
+
+def hybrid_layer_ops(layer):
+    """(kind, K, N) ops of one decoder layer in execution order; kind 'attn' is the paged decode attention."""
+    if layer in HYBRID_ATTN_LAYERS:
+        ops = [("qkv", 4096, 6144), ("attn", 0, 0), ("o_proj", 4096, 4096)]
+    else:
+        ops = [("in_proj_qkvz", 4096, 12288), ("in_proj_ba", 4096, 64), ("out_proj", 4096, 4096)]
+    return ops + [("gate_up", 4096, 24576), ("down", 12288, 4096)]
+
+
+def decode_step_bench(dev, quick=False):
+    """Hot-path share of one hybrid-model decode step: every linear (exact: digitize + exact GEMM; plain: cuBLAS bf16
+    x @ w.T) and the 8 paged-attention calls (the same batch-invariant kernel in both arms: attention reads the
+    same KV bytes either way), with distinct random weights per layer (14.8 GB of digits) and a separate paged KV
+    cache per attention layer. GDN recurrence, norms, RoPE and sampling are vLLM's and identical in both arms, so
+    they are left out: `exact_ms / plain_ms` bounds the step overhead of exactness from above. One CUDA graph per
+    step, replayed."""
+    import torch
+    import recipes as R
+    from vllm_exact import kernels as KK, paged_attn as PA
+    PA.MAX_LEN = 20480
+    stream = torch.cuda.Stream(dev)
+    g = torch.Generator(device=dev).manual_seed(5)
+    Wd, Wb = [], []
+    for layer in range(32):
+        d, b = {}, {}
+        for kind, K, N in hybrid_layer_ops(layer):
+            if kind == "attn":
+                continue
+            w = (torch.randn(N, K, generator=g, device=dev) * 0.02).bfloat16()
+            d[kind], b[kind] = KK.digitize_weight(w, 14), w
+        Wd.append(d)
+        Wb.append(b)
+    w = (torch.randn(151936, 4096, generator=g, device=dev) * 0.02).bfloat16()
+    lm_d, lm_b = KK.digitize_weight(w, 14), w
+    del w
+    res = {}
+    for n, ctx in (STEP_CONFIGS[:1] if quick else STEP_CONFIGS):
+        xs = {K: make_activation(n, K, K, dev) for K in (4096, 12288)}
+        ys = {}
+        caches = []
+        for i, layer in enumerate(HYBRID_ATTN_LAYERS):
+            q, kv, bt, sl = [t.to(dev) for t in R.paged_case(n, ctx, 16, 32, 8, 128, seed=i, ctx_jitter=True)]
+            kc, vc = R.kv_views(kv, 128)
+            caches.append((q, kv, kc, vc, bt, sl, torch.empty(n, 32, 128, device=dev, dtype=torch.bfloat16),
+                           torch.empty(PA.workspace_bytes(n, 32, 128), dtype=torch.uint8, device=dev)))
+
+        def out(kind, N):
+            if (kind, N) not in ys:
+                ys[(kind, N)] = torch.empty(n, N, device=dev, dtype=torch.bfloat16)
+            return ys[(kind, N)]
+
+        def step(exact):
+            ai = 0
+            for layer in range(32):
+                for kind, K, N in hybrid_layer_ops(layer):
+                    if kind == "attn":
+                        q, kv, kc, vc, bt, sl, o, ws = caches[ai]
+                        PA.paged_decode(q, kc, vc, bt, sl, 128 ** -0.5, o, n, workspace=ws)
+                        ai += 1
+                    elif exact:
+                        KK.exact_linear(KK.digitize(xs[K], 14), Wd[layer][kind], 14, True, out=out(kind, N))
+                    else:
+                        torch.matmul(xs[K], Wb[layer][kind].t(), out=out(kind, N))
+            if exact:
+                KK.exact_linear(KK.digitize(xs[4096], 14), lm_d, 14, True, out=out("lm_head", 151936))
+            else:
+                torch.matmul(xs[4096], lm_b.t(), out=out("lm_head", 151936))
+
+        KK.reserve_workspace(max(KK.lib().ex_linear_workspace_bytes(n, N, K, 0, 0)
+                                 for layer in range(32) for kind, K, N in hybrid_layer_ops(layer) if kind != "attn"),
+                             dev, stream=stream)
+        times = {}
+        for exact in (True, False):
+            with torch.cuda.stream(stream):
+                step(exact)
+            torch.cuda.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                step(exact)
+            for _ in range(3):
+                gr.replay()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 10
+            with torch.cuda.stream(stream):
+                a.record()
+                for _ in range(reps):
+                    gr.replay()
+                b.record()
+            torch.cuda.synchronize()
+            times[exact] = a.elapsed_time(b) / reps
+            del gr
+        res[f"b{n}/{ctx // 1024}K"] = {"exact_ms": round(times[True], 3), "plain_bf16_ms": round(times[False], 3),
+                                       "overhead": round(times[True] / times[False] - 1, 3)}
+        del caches, xs, ys
+        torch.cuda.empty_cache()
+    return res
+
+
 def cpu_baseline(W=None, budget_s=20.0):
     """The reference's CPU integer path, restated in oracle/ (numpy; integer dot products as exact float64 BLAS
     products), on a bounded sample of the decode sweep: every (M, shape) with the output columns capped at 2048
@@ -483,6 +592,8 @@ def run_case(args):
                     y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
                     KK.exact_linear(KK.digitize(make_activation(M, K, 17 * M + i, dev), 14), W[name], 14, True,
                                     out=y)
+    elif kind == "step":
+        print(json.dumps(decode_step_bench(dev)), flush=True)
     elif kind == "attn":
         n, ctx = int(rest[0]), int(rest[1])
         PA.MAX_LEN = 20480
@@ -497,6 +608,97 @@ def run_case(args):
     print(f"case {args.case} done")
 
 
+REF_TRITON_CFGS = sorted({(16, 64, 256, 4, 3, 8, 1), (16, 64, 256, 4, 3, 8, 4), (16, 128, 128, 4, 4, 8, 1),
+                          (16, 128, 128, 4, 4, 8, 2), (16, 128, 128, 4, 4, 8, 4), (64, 64, 128, 4, 3, 8, 1),
+                          (64, 64, 128, 4, 3, 8, 2), (64, 64, 128, 4, 3, 8, 4), (128, 128, 128, 8, 3, 8, 1),
+                          (64, 128, 128, 4, 4, 8, 1)})
+
+
+def _load_reference_module(name):
+    """Import a module of the reference package installed (git-ignored) under baseline/_ref, under a private name so
+    it cannot clash with this repository's vllm_exact package."""
+    import importlib.util
+    path = ROOT / "baseline" / "_ref" / "vllm_exact" / f"{name}.py"
+    if not path.exists():
+        raise SystemExit(f"reference not installed at {path.parent}")
+    spec = importlib.util.spec_from_file_location(f"reference_vllm_exact_{name}", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def run_ref_triton(args):
+    """Informational comparison on one B200: the reference's own Triton kernels (kernels.py _exact_kernel /
+    _exact_bf16_kernel, paged_attn.py _paged_partial/_paged_merge) against ours on identical inputs, both timed with
+    CUDA graphs that rotate the five weight matrices (so weights stream from HBM). For each GEMM shape the reference
+    runs its best of the tile configurations of its shipped B300 table and defaults, with INT8 and bf16 MMA; every
+    reference output is also checked bitwise against ours."""
+    import torch
+    from vllm_exact import kernels as KK, paged_attn as PA
+    import recipes as R
+    RK = _load_reference_module("kernels")
+    RP = _load_reference_module("paged_attn")
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.Stream(dev)
+    hbm = peaks()[0]
+    W = {name: make_weight_digits(K, N, 1000 + i, dev) for i, (name, K, N) in enumerate(SHAPES)}
+    out = {"gemm": {}, "attention": {}}
+    for M in DECODE_M + [256]:
+        xs = {name: KK.digitize(make_activation(M, K, 17 * M + i, dev), 14) for i, (name, K, N) in enumerate(SHAPES)}
+        ours_y = {name: torch.empty(M, N, device=dev, dtype=torch.bfloat16) for name, K, N in SHAPES}
+        KK.reserve_workspace(max(KK.lib().ex_linear_workspace_bytes(M, N, K, 0, 0) for _, K, N in SHAPES), dev,
+                             stream=stream)
+        fns = [(lambda n=name: KK.exact_linear(xs[n], W[n], 14, True, out=ours_y[n])) for name, K, N in SHAPES]
+        _, ours_ms = _graph_time(fns, 10, stream)
+        best = {}
+        for cfg in REF_TRITON_CFGS:
+            for mma in (0, 1):
+                c = cfg + (mma,)
+                if c[0] > max(16, 1 << max(0, (M - 1).bit_length())):
+                    continue
+                ys = {name: torch.empty(M, N, device=dev, dtype=torch.bfloat16) for name, K, N in SHAPES}
+                rf = [(lambda n=name, c=c: RK.exact_linear(xs[n], W[n], 14, True, out=ys[n], cfg=c))
+                      for name, K, N in SHAPES]
+                try:
+                    _, ref_ms = _graph_time(rf, 5, stream)
+                except Exception as e:  # a config that does not compile here
+                    print(f"reference cfg {c} failed: {type(e).__name__}", file=sys.stderr)
+                    continue
+                for (name, K, N), ms in zip(SHAPES, ref_ms):
+                    same = bool(torch.equal(ys[name], ours_y[name]))
+                    if name not in best or ms < best[name][0]:
+                        best[name] = (ms, c, same)
+                    elif not same:
+                        best[name] = (best[name][0], best[name][1], False)
+        for (name, K, N), ms in zip(SHAPES, ours_ms):
+            rms, rc, same = best[name]
+            by = gemm_bytes(M, K, N)
+            out["gemm"][f"{name}/M{M}"] = {"ours_us": round(ms * 1e3, 1), "ref_us": round(rms * 1e3, 1),
+                                           "speedup": round(rms / ms, 2), "ours_GBps": round(by / ms / 1e6, 1),
+                                           "ref_GBps": round(by / rms / 1e6, 1), "ref_cfg": list(rc),
+                                           "bitwise_equal": same}
+        print(json.dumps({f"M{M}": {k: v for k, v in out["gemm"].items() if k.endswith(f"/M{M}")}}), file=sys.stderr)
+    PA.MAX_LEN = RP.MAX_LEN = 20480
+    for n, ctx in ATTN:
+        q, kv, bt, sl = [t.to(dev) for t in R.paged_case(n, ctx, 16, 32, 8, 128, ctx_jitter=True)]
+        kc, vc = R.kv_views(kv, 128)
+        o1 = torch.empty(n, 32, 128, device=dev, dtype=torch.bfloat16)
+        o2 = torch.empty_like(o1)
+        ws = torch.empty(PA.workspace_bytes(n, 32, 128), dtype=torch.uint8, device=dev)
+        _, (ms1,) = _graph_time([lambda: PA.paged_decode(q, kc, vc, bt, sl, 128 ** -0.5, o1, n, workspace=ws)], 10,
+                                stream)
+        msl = int(sl.max())
+        _, (ms2,) = _graph_time([lambda: RP.paged_decode(q, kc, vc, bt, sl, 128 ** -0.5, o2, n, msl)], 10, stream)
+        L = int(sl.sum())
+        by = L * 8 * 128 * 2 * 2 + 2 * n * 32 * 128 * 2 + sum((int(l) + 15) // 16 for l in sl.tolist()) * 4 + 4 * n
+        out["attention"][f"b{n}/{ctx // 1024}K"] = {
+            "ours_us": round(ms1 * 1e3, 1), "ref_us": round(ms2 * 1e3, 1), "speedup": round(ms2 / ms1, 2),
+            "ours_frac_hbm": round(by / ms1 / 1e6 / hbm, 3), "ref_frac_hbm": round(by / ms2 / 1e6 / hbm, 3),
+            "max_abs_diff": float((o1.float() - o2.float()).abs().max())}
+        del kv
+    print(json.dumps({"ref_triton": out}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -506,7 +708,12 @@ def main():
     ap.add_argument("--quick", action="store_true", help="skip the slow secondary measurements")
     ap.add_argument("--case", default=None, help="profiling workload, e.g. gemm:o_proj:64 or attn:64:8192")
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--ref-triton", action="store_true",
+                    help="time the reference's Triton kernels (installed under baseline/_ref) against ours")
     args = ap.parse_args()
+    if args.ref_triton:
+        run_ref_triton(args)
+        return
     if args.case:
         run_case(args)
         return

@@ -73,19 +73,32 @@ struct TcSeg {
   int tile, kb, ke;
 };
 
-// Segment walker shared by all roles: CTA c owns k-iterations [c*T/G, (c+1)*T/G).
+// Segment walker shared by all roles: CTA c owns k-iterations [c*T/G, (c+1)*T/G). 32-bit arithmetic whenever
+// T*G fits (every decode and prefill shape here): 64-bit divisions cost ~1 us of prologue.
 struct TcWalk {
   int64_t it, it1;
   int KI;
   __device__ TcWalk(const TcArgs& a) {
-    it = (a.T * (int64_t)blockIdx.x) / a.G;
-    it1 = (a.T * (int64_t)(blockIdx.x + 1)) / a.G;
+    if (a.T * (int64_t)a.G < 2147483647ll) {
+      const uint32_t T = (uint32_t)a.T, G = (uint32_t)a.G, b = blockIdx.x;
+      it = (int64_t)((T * b) / G);
+      it1 = (int64_t)((T * (b + 1)) / G);
+    } else {
+      it = (a.T * (int64_t)blockIdx.x) / a.G;
+      it1 = (a.T * (int64_t)(blockIdx.x + 1)) / a.G;
+    }
     KI = a.KI;
   }
   __device__ bool next(TcSeg& s) {
     if (it >= it1) return false;
-    s.tile = (int)(it / KI);
-    s.kb = (int)(it % KI);
+    if (it < 2147483647ll) {
+      const uint32_t u = (uint32_t)it, k = (uint32_t)KI;
+      s.tile = (int)(u / k);
+      s.kb = (int)(u % k);
+    } else {
+      s.tile = (int)(it / KI);
+      s.kb = (int)(it % KI);
+    }
     s.ke = (int)min((int64_t)KI, (int64_t)s.kb + (it1 - it));
     it += s.ke - s.kb;
     return true;
@@ -371,7 +384,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const bool whole = (sg.kb == 0 && sg.ke == a.KI);
       // A split tile owns workspace slot b* = the first CTA boundary strictly inside it; every contributor computes
       // the same b*, distinct split tiles get distinct slots, and b* < G. Slot layout: [lane quarter][token][32 rows].
-      const int slot = whole ? 0 : (int)((((int64_t)sg.tile * a.KI + 1) * a.G + a.T - 1) / a.T);
+      int slot = 0;
+      if (!whole) {
+        const int64_t num = ((int64_t)sg.tile * a.KI + 1) * a.G + a.T - 1;
+        slot = num < 2147483647ll ? (int)((uint32_t)num / (uint32_t)a.T) : (int)(num / a.T);
+      }
       long long* slot_q = a.ws_acc + ((int64_t)slot * 4 + q) * BT * 32;
       const uint32_t t_hh = tmem_base + lane_off + (uint32_t)(buf * cb);
       if (half >= NCH) {  // no chunk for this warp (BT = 8): release the accumulator right away
