@@ -44,8 +44,11 @@ constexpr int TC_TOK_WORDS = TC_EPI_WARPS * 2 * 128 * 4;                // per w
 struct TcPlan {
   int BT;        // token tile
   int m_tiles, n_tiles, KI;
-  int64_t T;     // total k-iterations = tiles * KI
-  int G;         // CTAs
+  int64_t T;     // k-iterations of one m-tile row of tiles = n_tiles * KI
+  int gs;        // CTAs per group (one per m-tile of a chunk)
+  int groups;    // groups; group g walks (n-tile, k) range [T*g/groups, T*(g+1)/groups)
+  int chunks;    // passes over the range: m-tiles c*gs + j for c < chunks
+  int G;         // CTAs = groups * gs
   int stages;
   size_t smem;
   size_t ws_bytes;
@@ -63,52 +66,66 @@ struct TcArgs {
   int* ws_cnt;
   int M, N, K;
   int F, trunc, out_dtype, partial;
-  int m_tiles, KI;
-  int64_t T;
-  int G;
+  int m_tiles, n_tiles, KI;
+  int64_t T;  // n_tiles * KI
+  int gs, groups, chunks;
   int stages;
 };
 
 struct TcSeg {
-  int tile, kb, ke;
+  int m_tile, n_tile, kb, ke;
 };
 
-// Segment walker shared by all roles: CTA c owns k-iterations [c*T/G, (c+1)*T/G). 32-bit arithmetic whenever
-// T*G fits (every decode and prefill shape here): 64-bit divisions cost ~1 us of prologue.
+// Segment walker shared by all roles. CTAs form groups of gs siblings; sibling j of group g walks the (n-tile,
+// k-iteration) range [T*g/groups, T*(g+1)/groups) once for each m-tile chunk c, on m-tile c*gs + j. Siblings run in
+// lockstep over the same weight k-slices, so a weight tile leaves HBM once per chunk and the other siblings read it
+// from L2 (one m-tile: the original one-range-per-CTA partition). 32-bit arithmetic whenever the products fit.
 struct TcWalk {
-  int64_t it, it1;
-  int KI;
+  int64_t r0, r1, it;
+  int KI, j, mc, chunks, gs, m_tiles;
   __device__ TcWalk(const TcArgs& a) {
-    if (a.T * (int64_t)a.G < 2147483647ll) {
-      const uint32_t T = (uint32_t)a.T, G = (uint32_t)a.G, b = blockIdx.x;
-      it = (int64_t)((T * b) / G);
-      it1 = (int64_t)((T * (b + 1)) / G);
+    const int g = blockIdx.x / a.gs;
+    j = blockIdx.x % a.gs;
+    if (a.T * (int64_t)a.groups < 2147483647ll) {
+      const uint32_t T = (uint32_t)a.T, G = (uint32_t)a.groups, b = (uint32_t)g;
+      r0 = (int64_t)((T * b) / G);
+      r1 = (int64_t)((T * (b + 1)) / G);
     } else {
-      it = (a.T * (int64_t)blockIdx.x) / a.G;
-      it1 = (a.T * (int64_t)(blockIdx.x + 1)) / a.G;
+      r0 = (a.T * (int64_t)g) / a.groups;
+      r1 = (a.T * (int64_t)(g + 1)) / a.groups;
     }
+    it = r0;
     KI = a.KI;
+    mc = 0;
+    chunks = a.chunks;
+    gs = a.gs;
+    m_tiles = a.m_tiles;
   }
   __device__ bool next(TcSeg& s) {
-    if (it >= it1) return false;
-    if (it < 2147483647ll) {
-      const uint32_t u = (uint32_t)it, k = (uint32_t)KI;
-      s.tile = (int)(u / k);
-      s.kb = (int)(u % k);
-    } else {
-      s.tile = (int)(it / KI);
-      s.kb = (int)(it % KI);
+    while (mc < chunks) {
+      const int m_tile = mc * gs + j;
+      if (m_tile >= m_tiles || it >= r1) {
+        ++mc;
+        it = r0;
+        continue;
+      }
+      if (it < 2147483647ll) {
+        const uint32_t u = (uint32_t)it, k = (uint32_t)KI;
+        s.n_tile = (int)(u / k);
+        s.kb = (int)(u % k);
+      } else {
+        s.n_tile = (int)(it / KI);
+        s.kb = (int)(it % KI);
+      }
+      s.m_tile = m_tile;
+      s.ke = (int)min((int64_t)KI, (int64_t)s.kb + (r1 - it));
+      it += s.ke - s.kb;
+      return true;
     }
-    s.ke = (int)min((int64_t)KI, (int64_t)s.kb + (it1 - it));
-    it += s.ke - s.kb;
-    return true;
+    return false;
   }
 };
 
-// Epilogue of CW consecutive tokens m0+j (j < CW, t < M) of weight row n: F = 15 offset correction over the call's K,
-// then the raw int64 total (partial mode) or the scaled, rounded output. The per-row and per-token scale words are
-// loaded once, up front, through the read-only path (interleaving them with the output stores would serialise a
-// memory round trip per element).
 // sxs / cxs: this tile's per-token scale words, already in shared memory; swn / cwn: this weight row's.
 template <int CW>
 __device__ __forceinline__ void tc_finish_chunk(const long long (&tot)[CW], int m0, int n, const int* sxs,
@@ -240,7 +257,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     TcSeg sg;
     int left = S;
     while (left > 0 && walk.next(sg)) {
-      const int n_tile = sg.tile / a.m_tiles;
+      const int n_tile = sg.n_tile;
       for (int kt = sg.kb; kt < sg.ke && left > 0; ++kt, --left) {
         tma_prefetch_l2_2d(&tm_wh, kt * TC_BK, n_tile * 128);
         tma_prefetch_l2_2d(&tm_wl, kt * TC_BK, n_tile * 128);
@@ -262,7 +279,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       int64_t issued = 0;
       bool ok = true;
       while (ok && walk.next(sg)) {
-        const int n_tile = sg.tile / a.m_tiles, m_tile = sg.tile % a.m_tiles;
+        const int n_tile = sg.n_tile, m_tile = sg.m_tile;
         for (int kt = sg.kb; kt < sg.ke; ++kt) {
           if (!mbar_wait(empty_bar + stage, phase ^ 1, EX_DEVERR_WAIT_SLOT)) {
             ok = false;
@@ -366,7 +383,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     while (walk.next(sg)) {
       const int buf = nbuf == 2 ? (seg_i & 1) : 0;
       const uint32_t use = nbuf == 2 ? (uint32_t)(seg_i >> 1) : (uint32_t)seg_i;
-      const int n_tile = sg.tile / a.m_tiles, m_tile = sg.tile % a.m_tiles;
+      const int n_tile = sg.n_tile, m_tile = sg.m_tile;
       const int n = n_tile * 128 + row;
       const int m0 = m_tile * BT;
       // scale words of this tile, fetched while the MMAs still run (global latency is long under full HBM load)
@@ -382,12 +399,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (!mbar_wait(tfull_bar + buf, use & 1, EX_DEVERR_WAIT_MMA)) break;
       tc_fence_after();
       const bool whole = (sg.kb == 0 && sg.ke == a.KI);
-      // A split tile owns workspace slot b* = the first CTA boundary strictly inside it; every contributor computes
-      // the same b*, distinct split tiles get distinct slots, and b* < G. Slot layout: [lane quarter][token][32 rows].
+      // Slot layout: [lane quarter][token][32 rows].
+      // A split tile (m, n) owns slot (b* - 1) * m_tiles + m, b* = the first group boundary strictly inside n's
+      // k-range: every contributor computes the same slot and distinct split tiles get distinct slots.
       int slot = 0;
       if (!whole) {
-        const int64_t num = ((int64_t)sg.tile * a.KI + 1) * a.G + a.T - 1;
-        slot = num < 2147483647ll ? (int)((uint32_t)num / (uint32_t)a.T) : (int)(num / a.T);
+        const int64_t num = ((int64_t)n_tile * a.KI + 1) * a.groups + a.T - 1;
+        const int bstar = num < 2147483647ll ? (int)((uint32_t)num / (uint32_t)a.T) : (int)(num / a.T);
+        slot = (bstar - 1) * a.m_tiles + m_tile;
       }
       long long* slot_q = a.ws_acc + ((int64_t)slot * 4 + q) * BT * 32;
       const uint32_t t_hh = tmem_base + lane_off + (uint32_t)(buf * cb);
@@ -551,20 +570,23 @@ static TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int split_k, int algo, in
   p.m_tiles = (int)((M + p.BT - 1) / p.BT);
   p.n_tiles = (int)((N + 127) / 128);
   p.KI = (int)((K + TC_BK - 1) / TC_BK);
-  const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles;
-  p.T = tiles * p.KI;
-  int64_t G = split_k > 0 ? tiles * split_k : (int64_t)sms;
-  G = std::max<int64_t>(1, std::min<int64_t>(G, p.T));
-  G = std::min<int64_t>(G, 2147483647);
-  p.G = (int)G;
+  p.T = (int64_t)p.n_tiles * p.KI;
+  p.gs = std::min(p.m_tiles, 8);
+  p.chunks = (p.m_tiles + p.gs - 1) / p.gs;
+  int64_t groups = split_k > 0 ? (int64_t)p.n_tiles * split_k : std::max<int64_t>(1, sms / p.gs);
+  groups = std::max<int64_t>(1, std::min<int64_t>(groups, p.T));
+  groups = std::min<int64_t>(groups, 2147483647 / p.gs);
+  p.groups = (int)groups;
+  p.G = p.groups * p.gs;
   const size_t stage = tc_stage_bytes(p.BT);
   const size_t overhead = 1024 + 256 + TC_RED_STAGING + TC_TOK_WORDS;  // alignment, barriers, staging, scale words
   p.stages = (int)std::min<size_t>(8, (TC_SMEM_BUDGET - overhead) / stage);
   p.smem = (size_t)p.stages * stage + overhead;
-  const bool aligned = (G <= tiles) && (tiles % G == 0);
-  p.cnt_bytes = (size_t)((G * 4 + 255) / 256 * 256);
-  p.ws_bytes = aligned ? 0 : p.cnt_bytes + (size_t)G * p.BT * 128 * 8;  // one int64 tile slot per CTA boundary
-  // (slot layout [4 lane quarters][BT tokens][32 rows]: each epilogue warp reduces contiguous 2 KB pieces)
+  const bool aligned = (groups <= p.n_tiles) && (p.n_tiles % groups == 0);  // every group covers whole n-tiles
+  const int64_t slots = (groups - 1) * (int64_t)p.m_tiles;  // one per (group boundary, m-tile)
+  p.cnt_bytes = (size_t)((slots * 4 + 255) / 256 * 256);
+  p.ws_bytes = (aligned || slots == 0) ? 0 : p.cnt_bytes + (size_t)slots * p.BT * 128 * 8;
+  // (slot layout [4 lane quarters][BT tokens][32 rows]: each epilogue warp reduces contiguous 1 KB pieces)
   return p;
 }
 
@@ -616,9 +638,12 @@ static cudaError_t launch_tc(const TcPlan& p, int F, int trunc, int out_dtype, c
   a.out_dtype = out_dtype;
   a.partial = PARTIAL ? 1 : 0;
   a.m_tiles = p.m_tiles;
+  a.n_tiles = p.n_tiles;
   a.KI = p.KI;
   a.T = p.T;
-  a.G = p.G;
+  a.gs = p.gs;
+  a.groups = p.groups;
+  a.chunks = p.chunks;
   a.stages = p.stages;
   switch (p.BT) {
     case 8: return launch_tc_bt<8>(p, a, mwh, mwl, mxh, mxl, st);
