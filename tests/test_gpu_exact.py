@@ -191,3 +191,33 @@ def test_k_slices_sum_exactly(K):
 def test_no_device_timeouts(K):
     from vllm_exact import _lib
     assert _lib.device_error() == 0
+
+
+def test_invariance_stress_config3(K):
+    """16 fixed target rows (K=12288, N=4096) embedded at random positions in batches of every
+    M in 1..256 (filler rows N(0,1) with 0.1 % x50 outliers, seed M), every split-K in {auto, 1, 2, 4, 8}: each
+    target row's bf16 output is bitwise identical in every setting (tensor-core kernel for every M, the SIMT kernel
+    for a subset). The 16 targets are checked once against the CPU oracle."""
+    Kd, N = 12288, 4096
+    targets = torch.randn(16, Kd, generator=torch.Generator().manual_seed(0))
+    w = torch.randn(N, Kd, generator=torch.Generator().manual_seed(1)) * 0.02
+    wd = K.digitize(w.bfloat16().to(DEV), 14)
+    td = K.digitize(targets.bfloat16().to(DEV), 14)
+    base = _run(K, td, wd, 14, True, "tc_i8", 1, torch.bfloat16)
+    ref = O.f32_to_bf16_bits(O.exact_linear(_digits_np(td), _digits_np(wd), 14, True))
+    assert np.array_equal(base.cpu().view(torch.int16).numpy().view(np.uint16), ref)
+    tg = targets.bfloat16().to(DEV)
+    for M in range(1, 257):
+        gm = torch.Generator(device=DEV).manual_seed(M)
+        filler = torch.randn(M, Kd, device=DEV, generator=gm)
+        filler[torch.rand(M, Kd, device=DEV, generator=gm) < 0.001] *= 50
+        filler = filler.bfloat16()
+        nt = min(M, 16)
+        pos = torch.randperm(M, device=DEV, generator=gm)[:nt]
+        filler[pos] = tg[:nt]
+        xd = K.digitize(filler, 14)
+        algos = ALGOS if M in (1, 2, 7, 16, 33, 64, 100, 256) else ["tc_i8"]
+        for algo in algos:
+            for sk in (0, 1, 2, 4, 8):
+                y = _run(K, xd, wd, 14, True, algo, sk, torch.bfloat16)
+                assert torch.equal(y[pos], base[:nt]), (M, algo, sk)

@@ -1,0 +1,56 @@
+"""The drop-in surface (reference __init__.py:32-68, plugin.py:105-133, paged_attn.py:135-163), each check in a fresh
+interpreter (tests/surface_driver.py) because enable() must run before vLLM is imported."""
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _run(mode, timeout=600):
+    p = subprocess.run([sys.executable, str(ROOT / "tests" / "surface_driver.py"), mode], capture_output=True,
+                       text=True, timeout=timeout, cwd=str(ROOT))
+    lines = [l for l in p.stdout.splitlines() if l.startswith("SURFACE_JSON ")]
+    assert p.returncode == 0 and lines, p.stdout[-2000:] + p.stderr[-4000:]
+    return json.loads(lines[-1][len("SURFACE_JSON "):])
+
+
+def test_enable_returns_reference_kwargs_and_installs_everything():
+    r = _run("enable")
+    assert r["kwargs"] == {"quantization": "exact_int8", "max_num_batched_tokens": 131072,
+                           "enable_prefix_caching": False, "additional_config": {"gdn_prefill_backend": "triton"},
+                           "attention_config": {"backend": "FLASH_ATTN"}}
+    assert r["env"] == ["1", "0"]
+    assert r["quant_config"] == "vllm_exact.plugin"
+    assert r["fa_forward_file"] == "paged_attn.py"
+    assert r["gdn_invariant"] is True
+    assert r["max_len"] == 20480
+    assert r["plugin"] == [14, True, True]
+    assert "only be called once" in r["second_call"]
+    assert r["custom_op"] == "exactmm.linear"
+
+
+def test_enable_after_vllm_import_is_refused():
+    code = ("import sys; sys.path.insert(0, 'vllm-exact_b200'); import vllm, vllm_exact\n"
+            "try:\n    vllm_exact.enable(max_model_len=16)\nexcept RuntimeError as e:\n    print('REFUSED', e)\n")
+    p = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600, cwd=str(ROOT))
+    assert "REFUSED" in p.stdout and "before importing vllm" in p.stdout
+
+
+@pytest.mark.gpu
+def test_plugin_methods_and_attention_patch_on_gpu():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    r = _run("plugin")
+    assert r["linear_method"] == "ExactLinearMethod"
+    assert r["lm_head_method"] == "ExactLMHeadMethod"
+    assert r["buffers"] == ["ex_cw", "ex_sw", "ex_wh", "ex_wl"]
+    assert r["shape"] == [2, 4, 1024]
+    assert r["config1_sha_ok"] is True
+    assert r["bias_ok"] is True
+    assert r["patch_matches_kernel"] is True and r["padding_untouched"] is True
+    assert r["patch_max_err"] < 1e-3
