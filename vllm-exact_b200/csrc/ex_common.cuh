@@ -51,21 +51,6 @@ __device__ __forceinline__ float ex_scale_to_f32(long long tot, int sx, int sw) 
   return __double2float_rn(__dmul_rn(__ll2double_rn(tot), scale));
 }
 
-// Same value as ex_scale_to_f32(tot, sx, sw) with e = -(sx + sw), in fewer instructions: round the integer to float32
-// once (__ll2float_rn rounds the exact integer to nearest even, as float64 -> float32 does, since |tot| < 2^53 makes
-// the float64 conversion exact), then multiply by 2^e by adding e to the exponent field. Scaling by a power of two
-// commutes with round-to-nearest whenever the result stays a normal float32, so the bits are identical there; results
-// that would be subnormal or overflow take the float64 path.
-__device__ __forceinline__ float ex_scale_to_f32_fast(long long tot, int sx, int sw) {
-  const float f = __ll2float_rn(tot);
-  const uint32_t b = __float_as_uint(f);
-  const int ef = (int)((b >> 23) & 0xFFu);
-  const int en = ef - sx - sw;
-  if (f == 0.0f) return f;
-  if (en >= 1 && en <= 254) return __uint_as_float((b & 0x807FFFFFu) | ((uint32_t)en << 23));
-  return ex_scale_to_f32(tot, sx, sw);
-}
-
 template <int OUT_DTYPE>
 __device__ __forceinline__ void ex_store_out(void* out, long long idx, float v) {
   if constexpr (OUT_DTYPE == EX_DTYPE_F32) {

@@ -1,7 +1,8 @@
 // Per-row fixed-point digitization (replaces kernels.py:46-85; semantics of digitize_torch, kernels.py:22-39).
 //
-// One CTA per row, two passes over the row: a max-|x| reduction, then the digits. HBM traffic per row:
-// K * sizeof(x) read (the second pass hits L1/L2) + 2K bytes of digits + 8 bytes of cs/sh written.
+// One CTA per row: a max-|x| reduction over the row, then the digits. Rows of up to 16384 aligned elements are held
+// in registers between the two steps (k_digitize_reg); longer or unaligned rows are read twice (k_digitize, the
+// second pass hits L1/L2). HBM traffic per row: K * sizeof(x) read + 2K bytes of digits + 8 bytes of cs/sh written.
 #pragma once
 #include "ex_common.cuh"
 
@@ -167,6 +168,75 @@ __global__ void __launch_bounds__(DIG_THREADS) k_digitize(const T* __restrict__ 
   }
 }
 
+// Register-resident variant for rows of at most NV * 8 * DIG_THREADS elements (aligned as for VEC): every thread
+// issues all of its loads before using any, the row maximum is reduced once, and the digits are made from the
+// registers, so a row costs one global round trip instead of one per loop iteration in each of two passes. The
+// digitizer sits between two GEMMs on the critical path of a decode step, where this latency is what counts.
+template <typename T, int F, int NV, int MODE>
+__global__ void __launch_bounds__(DIG_THREADS) k_digitize_reg(const T* __restrict__ x, int64_t ldx, int K,
+                                                              int8_t* __restrict__ h, int8_t* __restrict__ l,
+                                                              int64_t ldd, int32_t* __restrict__ cs,
+                                                              int32_t* __restrict__ sh, float* __restrict__ amax_io) {
+  __shared__ float redf[DIG_THREADS / 32];
+  __shared__ int redi[DIG_THREADS / 32];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * ldx;
+  float v[NV][8];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int k = (i * DIG_THREADS + (int)threadIdx.x) * 8;
+    if (k < K) {
+      load8<T>(xr + k, v[i]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[i][e] = 0.0f;
+    }
+  }
+  float amax = 0.0f;
+  if constexpr (MODE == DIG_GIVEN) {
+    amax = amax_io[row];
+  } else {
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[i][e]));
+    amax = block_max(amax, redf);
+  }
+  if constexpr (MODE == DIG_ABSMAX) {
+    if (threadIdx.x == 0) amax_io[row] = amax;
+    return;
+  }
+  const int s = F - frexp_exponent(amax);
+  const float scale = __uint_as_float(((uint32_t)(s + 127)) << 23);  // 2^s, int32 wrap-around as kernels.py:29
+  int csum = 0;
+  int8_t* hr = h + row * ldd;
+  int8_t* lr = l + row * ldd;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int k = (i * DIG_THREADS + (int)threadIdx.x) * 8;
+    if (k >= K) continue;
+    uint32_t hw[2] = {0, 0}, lw[2] = {0, 0};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int q = __float2int_rz(__fmul_rn(v[i][e], scale));
+      int dh, dl;
+      digits_of<F>(q, dh, dl);
+      if constexpr (F == 15) csum += 256 * dh + dl;
+      hw[e >> 2] |= ((uint32_t)(dh & 0xFF)) << (8 * (e & 3));
+      lw[e >> 2] |= ((uint32_t)(dl & 0xFF)) << (8 * (e & 3));
+    }
+    *reinterpret_cast<uint2*>(hr + k) = make_uint2(hw[0], hw[1]);
+    *reinterpret_cast<uint2*>(lr + k) = make_uint2(lw[0], lw[1]);
+  }
+  if constexpr (F == 15) csum = block_sum_i32(csum, redi);
+  if (threadIdx.x == 0) {
+    cs[row] = (F == 15) ? csum : 0;
+    sh[row] = s;
+  }
+}
+
 template <typename T, int F, int MODE>
 static cudaError_t launch_digitize_t(const void* x, int64_t ldx, int64_t rows, int64_t K, int8_t* h, int8_t* l,
                                      int64_t ldd, int32_t* cs, int32_t* sh, float* amax_io, cudaStream_t st) {
@@ -177,6 +247,15 @@ static cudaError_t launch_digitize_t(const void* x, int64_t ldx, int64_t rows, i
                    (MODE == DIG_ABSMAX || ((ldd % 8 == 0) && (reinterpret_cast<uintptr_t>(h) % 8 == 0) &&
                                            (reinterpret_cast<uintptr_t>(l) % 8 == 0)));
   dim3 grid((unsigned)rows);
+  constexpr int64_t PER_NV = 8 * DIG_THREADS;  // elements per register vector slot across the CTA
+#define EX_DIG_REG(NV)                                                                                              \
+  return ex_launch_pdl(k_digitize_reg<T, F, NV, MODE>, grid, dim3(DIG_THREADS), 0, st, xp, ldx, (int)K, h, l, ldd, \
+                       cs, sh, amax_io)
+  if (vec && K <= 1 * PER_NV) EX_DIG_REG(1);
+  if (vec && K <= 2 * PER_NV) EX_DIG_REG(2);
+  if (vec && K <= 4 * PER_NV) EX_DIG_REG(4);
+  if (vec && K <= 8 * PER_NV) EX_DIG_REG(8);
+#undef EX_DIG_REG
   if (vec)
     return ex_launch_pdl(k_digitize<T, F, true, MODE>, grid, dim3(DIG_THREADS), 0, st, xp, ldx, (int)K, h, l, ldd, cs,
                          sh, amax_io);

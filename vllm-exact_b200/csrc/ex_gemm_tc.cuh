@@ -14,17 +14,18 @@
 //   MMA3  D[ll]      (+)= Wl . Xl^T            (N = BT, only without truncation)
 // so md holds xh.wl + xl.wh directly. int32 is exact: |md| <= 2^15 K < 2^31 for K <= 65536.
 //
-// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer, warps 2..5 = epilogue
-// (TMEM -> registers -> int64 combine -> scale -> store). Two TMEM accumulator buffers let the epilogue of one
-// segment overlap the MMAs of the next.
+// Warp roles (320 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer, warps 2..9 = epilogue
+// (TMEM -> registers -> int64 combine -> scale -> store), two warps per TMEM lane quarter. Two TMEM accumulator
+// buffers let the epilogue of one segment overlap the MMAs of the next.
 //
-// Work partition: the (tile, k-iteration) space is flattened (tiles ordered n-major, m-minor so the m-tiles that
-// share a weight tile run back to back) and cut into G equal contiguous ranges, one per CTA. A CTA's range is a list
-// of segments (tile, k_begin, k_end). A segment covering a whole tile is written directly; otherwise its int64
-// totals are added with relaxed atomics into the tile's workspace slot (at most G - 1 tiles are split, one slot per
-// CTA boundary) and a ticket counting k-iterations elects the CTA that completes the tile, which applies the
-// epilogue and zeroes the slot again. Integer addition is exact and
-// order-free, so the result bits do not depend on G, on the split, or on arrival order.
+// Work partition: the (n-tile, k-iteration) space of one row of m-tiles is cut into `groups` equal contiguous
+// ranges; a group is gs sibling CTAs that walk the same range on gs different m-tiles in lockstep, so each weight
+// tile leaves HBM once and the siblings find it in L2. A CTA's walk is a list of segments (m-tile, n-tile, k_begin,
+// k_end). A segment covering a whole tile is finished straight from TMEM; otherwise its int64 totals are added with
+// bulk reduce-adds (TMA engine) into the tile's workspace slot (one slot per (group boundary, m-tile)) and a ticket
+// counting k-iterations elects the CTA that completes the tile, which applies the epilogue and zeroes the slot
+// again. Integer addition is exact and order-free, so the result bits do not depend on the partition or on arrival
+// order.
 #pragma once
 #include "ex_common.cuh"
 
@@ -127,50 +128,48 @@ struct TcWalk {
 };
 
 // sxs / cxs: this tile's per-token scale words, already in shared memory; swn / cwn: this weight row's.
+// All CW values are converted first with straight-line float64 code (ex_scale_to_f32: exact int64 -> float64, exact
+// power-of-two scaling, one rounding to float32; on sm_100 this is about twice as fast as an int64 -> float32
+// conversion, which is not a single hardware operation), then stored, predicated on the token count.
 template <int CW>
 __device__ __forceinline__ void tc_finish_chunk(const long long (&tot)[CW], int m0, int n, const int* sxs,
                                                 const int* cxs, int swn, long long cwn, const TcArgs& a) {
   if (n >= a.N) return;
-  const long long kc = 16384ll * (long long)a.K;
   const int jmax = min(CW, a.M - m0);
+  long long v[CW];
+  if (a.F == 15) {
+    const long long kc = 16384ll * (long long)a.K + 128ll * cwn;
+#pragma unroll
+    for (int j = 0; j < CW; ++j) v[j] = tot[j] + 128ll * (long long)cxs[j] + kc;
+  } else {
+#pragma unroll
+    for (int j = 0; j < CW; ++j) v[j] = tot[j];
+  }
   if (a.partial) {
     long long* op = reinterpret_cast<long long*>(a.out) + (int64_t)m0 * a.ldo + n;
 #pragma unroll
-    for (int j = 0; j < CW; ++j) {
-      if (j >= jmax) break;
-      long long v = tot[j];
-      if (a.F == 15) v += 128ll * ((long long)cxs[j] + cwn) + kc;
-      op[(int64_t)j * a.ldo] = v;
-    }
+    for (int j = 0; j < CW; ++j)
+      if (j < jmax) op[(int64_t)j * a.ldo] = v[j];
     return;
   }
+  float f[CW];
+#pragma unroll
+  for (int j = 0; j < CW; ++j) f[j] = ex_scale_to_f32(v[j], sxs[j], swn);
   if (a.out_dtype == EX_DTYPE_BF16) {
     __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(a.out) + (int64_t)m0 * a.ldo + n;
 #pragma unroll
-    for (int j = 0; j < CW; ++j) {
-      if (j >= jmax) break;
-      long long v = tot[j];
-      if (a.F == 15) v += 128ll * ((long long)cxs[j] + cwn) + kc;
-      op[(int64_t)j * a.ldo] = __float2bfloat16_rn(ex_scale_to_f32_fast(v, sxs[j], swn));
-    }
+    for (int j = 0; j < CW; ++j)
+      if (j < jmax) op[(int64_t)j * a.ldo] = __float2bfloat16_rn(f[j]);
   } else if (a.out_dtype == EX_DTYPE_F32) {
     float* op = reinterpret_cast<float*>(a.out) + (int64_t)m0 * a.ldo + n;
 #pragma unroll
-    for (int j = 0; j < CW; ++j) {
-      if (j >= jmax) break;
-      long long v = tot[j];
-      if (a.F == 15) v += 128ll * ((long long)cxs[j] + cwn) + kc;
-      op[(int64_t)j * a.ldo] = ex_scale_to_f32_fast(v, sxs[j], swn);
-    }
+    for (int j = 0; j < CW; ++j)
+      if (j < jmax) op[(int64_t)j * a.ldo] = f[j];
   } else {
     __half* op = reinterpret_cast<__half*>(a.out) + (int64_t)m0 * a.ldo + n;
 #pragma unroll
-    for (int j = 0; j < CW; ++j) {
-      if (j >= jmax) break;
-      long long v = tot[j];
-      if (a.F == 15) v += 128ll * ((long long)cxs[j] + cwn) + kc;
-      op[(int64_t)j * a.ldo] = __float2half_rn(ex_scale_to_f32_fast(v, sxs[j], swn));
-    }
+    for (int j = 0; j < CW; ++j)
+      if (j < jmax) op[(int64_t)j * a.ldo] = __float2half_rn(f[j]);
   }
 }
 
@@ -201,7 +200,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // 1024-byte alignment for the 128-byte-swizzled tiles
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = a.stages;
-  // per epilogue warp, two 2 KB staging buffers (8 tokens x 32 rows of int64) for bulk reduce-adds of split tiles
+  // per epilogue warp, two 1 KB staging buffers (4 tokens x 32 rows of int64) for bulk reduce-adds of split tiles
   long long* stage_red = reinterpret_cast<long long*>(smem + (size_t)S * Lay::STAGE);
   // per epilogue warp: the current tile's per-token shifts and row sums (2 x BT int32)
   int* tok_words = reinterpret_cast<int*>(smem + (size_t)S * Lay::STAGE + TC_RED_STAGING);
@@ -432,7 +431,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           for (int j = 0; j < CW; ++j) tot[j] = ex_combine((int)vh[j], (int)vm[j], a.trunc ? 0 : (int)vl[j]);
           tc_finish_chunk<CW>(tot, m0 + c, n, my_sx + c, my_cx + c, swn, cwn, a);
         } else {
-          // stage 4 tokens x 32 rows in shared memory, then one 1 KB bulk reduce-add into the slot (TMA engine)
+          // Stage 4 tokens x 32 rows in shared memory, then one 1 KB bulk reduce-add into the slot (TMA engine).
+          // Per-element atomics from registers measured slower on wide layers: the adds of a CTA's first split
+          // segment then compete with the weight stream in L2, where the bulk engine's do not.
 #pragma unroll
           for (int j0 = 0; j0 < CW; j0 += TC_RED_TOK) {
             long long* sb = my_stage + (size_t)(nbulk & 1) * TC_RED_TOK * 32;
