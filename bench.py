@@ -575,12 +575,13 @@ def run_case(args):
     kind, *rest = args.case.split(":")
     if kind == "gemm":
         name, M = rest[0], int(rest[1])
-        algo = {"tc_i8": KK.EX_ALGO_TC_I8, "simt": KK.EX_ALGO_SIMT, "auto": KK.EX_ALGO_AUTO}[rest[2] if len(rest) > 2
-                                                                                            else "auto"]
+        algo = {"tc_i8": KK.EX_ALGO_TC_I8, "tc_pair": KK.EX_ALGO_TC_I8_PAIR, "simt": KK.EX_ALGO_SIMT,
+                "auto": KK.EX_ALGO_AUTO}[rest[2] if len(rest) > 2 else "auto"]
         (K, N), = [(k, n) for nm, k, n in SHAPES if nm == name]
         W = make_weight_digits(K, N, 1, dev)
         xd = KK.digitize(make_activation(M, K, 2, dev), 14)
         y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+        KK.reserve_workspace(KK.lib().ex_linear_workspace_bytes(M, N, K, 0, algo), dev)
         for _ in range(args.reps):
             KK.exact_linear(xd, W, 14, True, out=y, cfg={"algo": algo})
     elif kind == "sweep":

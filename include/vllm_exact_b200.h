@@ -45,7 +45,8 @@ enum {
   EX_ALGO_AUTO = 0,    /* pick by shape */
   EX_ALGO_SIMT = 1,    /* CUDA cores, int8 dp4a, int32 accumulation */
   EX_ALGO_TC_I8 = 2,   /* tcgen05 kind::i8 tensor cores, TMA-fed, int32 accumulators in tensor memory */
-  EX_ALGO_TC_BF16 = 3  /* tcgen05 kind::f16 tensor cores on bf16-converted digits, fp32 accumulators drained to int */
+  EX_ALGO_TC_BF16 = 3, /* tcgen05 kind::f16 tensor cores on bf16-converted digits, fp32 accumulators drained to int */
+  EX_ALGO_TC_I8_PAIR = 4 /* tcgen05 kind::i8 on CTA pairs (cta_group::2, 256 weight rows x 128 tokens per pair tile) */
 };
 
 const char* ex_version(void);

@@ -12,7 +12,7 @@ from oracle import exact_oracle as O
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-ALGOS = ["simt", "tc_i8"]
+ALGOS = ["simt", "tc_i8", "tc_pair"]
 
 
 @pytest.fixture(scope="module")
@@ -24,7 +24,8 @@ def K():
 
 
 def _algo(K, name):
-    return {"simt": K.EX_ALGO_SIMT, "tc_i8": K.EX_ALGO_TC_I8, "auto": K.EX_ALGO_AUTO}[name]
+    return {"simt": K.EX_ALGO_SIMT, "tc_i8": K.EX_ALGO_TC_I8, "tc_pair": K.EX_ALGO_TC_I8_PAIR,
+            "auto": K.EX_ALGO_AUTO}[name]
 
 
 def _np(t):

@@ -151,7 +151,7 @@ int linear_impl(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* 
                                             (int)N, (int)K, p, out, ldo, workspace, st));
   }
   if (algo == EX_ALGO_TC_BF16) return EX_ERR_UNSUPPORTED;
-  if (algo == EX_ALGO_TC_I8) {
+  if (algo == EX_ALGO_TC_I8 || algo == EX_ALGO_TC_I8_PAIR) {
     if (!ex::tc_supported(xh, xl, ldx, wh, wl, ldw, M, N, K)) return EX_ERR_ALIGN;
     const ex::TcPlan p = ex::tc_plan(M, N, K, split_k, algo, num_sms());
     if (p.ws_bytes > 0 && (!workspace || workspace_bytes < p.ws_bytes)) return EX_ERR_WORKSPACE;
@@ -217,10 +217,13 @@ int launch_merge(const float* ws_m, const float* ws_l, const float* ws_acc, void
 
 size_t linear_ws(int64_t M, int64_t N, int64_t K, int split_k, int algo) {
   if (M <= 0 || N <= 0) return 0;
-  if (algo == EX_ALGO_AUTO) algo = EX_ALGO_TC_I8;  // TC plans need at least as much as SIMT ones, sized generously
   size_t a = simt_plan(M, N, K, split_k).ws_bytes;
-  size_t b = (algo == EX_ALGO_SIMT) ? 0 : ex::tc_plan(M, N, K, split_k, algo, num_sms()).ws_bytes;
-  return std::max(a, b);
+  if (algo == EX_ALGO_SIMT) return a;
+  if (algo != EX_ALGO_AUTO) return std::max(a, ex::tc_plan(M, N, K, split_k, algo, num_sms()).ws_bytes);
+  // automatic choice: enough for whichever tensor-core plan it may pick
+  const size_t b = ex::tc_plan(M, N, K, split_k, EX_ALGO_TC_I8, num_sms()).ws_bytes;
+  const size_t c = ex::tc_plan(M, N, K, split_k, EX_ALGO_TC_I8_PAIR, num_sms()).ws_bytes;
+  return std::max(a, std::max(b, c));
 }
 
 }  // namespace
@@ -316,7 +319,8 @@ int ex_linear_noalloc(const int8_t* xh, const int8_t* xl, int64_t ldx, const int
   size_t need = 0;
   if (chosen == EX_ALGO_SIMT)
     need = simt_plan(M, N, K, split_k).ws_bytes;
-  else if (chosen == EX_ALGO_TC_I8 && ex::tc_supported(xh, xl, ldx, wh, wl, ldw, M, N, K))
+  else if ((chosen == EX_ALGO_TC_I8 || chosen == EX_ALGO_TC_I8_PAIR) &&
+           ex::tc_supported(xh, xl, ldx, wh, wl, ldw, M, N, K))
     need = ex::tc_plan(M, N, K, split_k, chosen, num_sms()).ws_bytes;
   if (need > EX_NOALLOC_SCRATCH_BYTES) {
     g_last_error = "ex_linear_noalloc: this shape's split-K plan needs " + std::to_string(need) +

@@ -11,7 +11,7 @@ LIB_PATH = Path(os.environ.get("VLLM_EXACT_B200_LIB", Path(__file__).with_name("
 
 EX_OK, EX_ERR_ARG, EX_ERR_ALIGN, EX_ERR_WORKSPACE, EX_ERR_DTYPE, EX_ERR_UNSUPPORTED, EX_ERR_CUDA, EX_ERR_DEVICE = range(8)
 EX_DTYPE_F32, EX_DTYPE_BF16, EX_DTYPE_F16 = 0, 1, 2
-EX_ALGO_AUTO, EX_ALGO_SIMT, EX_ALGO_TC_I8, EX_ALGO_TC_BF16 = 0, 1, 2, 3
+EX_ALGO_AUTO, EX_ALGO_SIMT, EX_ALGO_TC_I8, EX_ALGO_TC_BF16, EX_ALGO_TC_I8_PAIR = 0, 1, 2, 3, 4
 
 c_i64, c_i32, c_vp, c_sz, c_f32 = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_float
 

@@ -23,10 +23,11 @@ import threading
 import torch
 
 from . import _lib
-from ._lib import EX_ALGO_AUTO, EX_ALGO_SIMT, EX_ALGO_TC_BF16, EX_ALGO_TC_I8, check, lib
+from ._lib import EX_ALGO_AUTO, EX_ALGO_SIMT, EX_ALGO_TC_BF16, EX_ALGO_TC_I8, EX_ALGO_TC_I8_PAIR, check, lib
 
 __all__ = ["digitize", "digitize_weight", "exact_linear", "exact_linear_partial_i64", "exact_epilogue",
-           "reserve_workspace", "EX_ALGO_AUTO", "EX_ALGO_SIMT", "EX_ALGO_TC_I8", "EX_ALGO_TC_BF16"]
+           "reserve_workspace", "EX_ALGO_AUTO", "EX_ALGO_SIMT", "EX_ALGO_TC_I8", "EX_ALGO_TC_BF16",
+           "EX_ALGO_TC_I8_PAIR"]
 
 _DT = {torch.float32: _lib.EX_DTYPE_F32, torch.bfloat16: _lib.EX_DTYPE_BF16, torch.float16: _lib.EX_DTYPE_F16}
 _LD_ALIGN = 16  # digit rows are padded to 16 bytes so the tensor-core kernels can TMA them
