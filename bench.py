@@ -42,7 +42,7 @@ ATTN = [(256, 1024), (64, 8192), (16, 16384)]
 METRIC = "exact-GEMM TB/s (exact_int8 linear, decode shapes M<=64 of the configs[1] sweep)"
 # DRAM bytes (read + write) per k_exact_tc_i8 launch, averaged over the 15 launches of one decode step, from the ncu
 # capture summarised in profiles/k_exact_tc_i8__decode_sweep.md (1.009 x the algorithmic bytes).
-GEMM_TRAFFIC_PER_LAUNCH = 331_666_637
+GEMM_TRAFFIC_PER_LAUNCH = 331_717_905
 
 
 def peaks():
