@@ -564,10 +564,122 @@ def run_reference(args):
     }), flush=True)
 
 
+ENGINE_MAX_LEN = 21504  # prompts up to 1.25 x 16K plus 321 generated tokens
+
+
+def _engine_model_dir():
+    """config.json of BASELINE configs[4]'s model: the qwen3_5 text architecture with hidden 4096, 32 layers (24
+    Gated-DeltaNet + 8 full attention, GQA 32q/8kv x 128), SwiGLU 12288, vocab 151936; GDN heads give in_proj_qkvz
+    N = 12288 and in_proj_ba N = 64 (the reference's tuned shapes). Weights are vLLM's dummy (random) init."""
+    import json
+    import tempfile
+    cfg = {"architectures": ["HybridQwen35ForCausalLM"], "model_type": "qwen3_5_text", "hidden_size": 4096,
+           "intermediate_size": 12288, "num_hidden_layers": 32, "num_attention_heads": 32, "num_key_value_heads": 8,
+           "head_dim": 128, "vocab_size": 151936, "linear_num_key_heads": 16, "linear_num_value_heads": 32,
+           "linear_key_head_dim": 128, "linear_value_head_dim": 128, "linear_conv_kernel_dim": 4,
+           "full_attention_interval": 4, "max_position_embeddings": 32768, "rms_norm_eps": 1e-6,
+           "rope_parameters": {"rope_type": "default", "rope_theta": 10000000.0, "partial_rotary_factor": 0.25},
+           "tie_word_embeddings": False, "torch_dtype": "bfloat16", "hidden_act": "silu", "eos_token_id": 151643}
+    d = tempfile.mkdtemp(prefix="exact_engine_")
+    with open(f"{d}/config.json", "w") as f:
+        json.dump(cfg, f)
+    return d
+
+
+def _register_engine_model():
+    """vLLM 0.22 ships the text-only Qwen3.5 model class without the hybrid (GDN state) interface that only its
+    vision-language twin declares; give it that interface (the twin's own state-shape hooks) and register it."""
+    from vllm import ModelRegistry
+    from vllm.model_executor.models.interfaces import IsHybrid
+    from vllm.model_executor.models.qwen3_5 import Qwen3_5ForCausalLM, Qwen3_5ForConditionalGeneration as VL
+
+    class HybridQwen35ForCausalLM(Qwen3_5ForCausalLM, IsHybrid):
+        get_mamba_state_dtype_from_config = classmethod(VL.get_mamba_state_dtype_from_config.__func__)
+        get_mamba_state_shape_from_config = classmethod(VL.get_mamba_state_shape_from_config.__func__)
+        get_mamba_state_copy_func = classmethod(VL.get_mamba_state_copy_func.__func__)
+
+    ModelRegistry.register_model("HybridQwen35ForCausalLM", HybridQwen35ForCausalLM)
+
+
+def engine_case(args):
+    """BASELINE configs[4] through the real vLLM engine: `engine:exact` (vllm_exact.enable(), every linear and the
+    lm_head exact_int8, decode attention patched) or `engine:plain` (stock non-invariant bf16 vLLM), same model, dummy
+    weights, random-token prompts, both arms with vLLM's engine core in-process (enable() requires it; the plain arm
+    is given the same setting). Follows the reference's scripts/check_invariance.py: invariance = 16 targets with
+    1,024-token prompts, alone (A), interleaved into a batch of 64 (B), alone again (C), 256 generated tokens, greedy
+    and temperature 1.0 (top-k 20, top-p 0.95, per-request seeds), tokens and logprobs compared bitwise; speed =
+    (t(321 new tokens) - t(65 new tokens)) / 256 with the minimum of two runs each, at (256, 1K), (64, 8K), (16, 16K),
+    prompt lengths uniform in [0.75, 1.25] x ctx. Prints one JSON line. One arm per process."""
+    import random
+    import time
+    arm = args.case.split(":")[1] if ":" in args.case else "exact"
+    kw = {}
+    if arm == "exact":
+        import vllm_exact
+        kw = vllm_exact.enable(max_model_len=ENGINE_MAX_LEN)
+    else:
+        os.environ["VLLM_ENABLE_V1_MULTIPROCESSING"] = "0"
+        kw = {"enable_prefix_caching": False}
+    _register_engine_model()
+    from vllm import LLM, SamplingParams
+    t0 = time.time()
+    llm = LLM(model=_engine_model_dir(), load_format="dummy", skip_tokenizer_init=True, dtype="bfloat16",
+              max_model_len=ENGINE_MAX_LEN, gpu_memory_utilization=0.85, max_num_seqs=256, seed=0, **kw)
+    res = {"arm": arm, "startup_s": round(time.time() - t0, 1), "invariance": {}, "speed": {}}
+
+    def prompts_of(n, lo, hi, seed):
+        rng = random.Random(seed)
+        return [[rng.randrange(100, 150000) for _ in range(rng.randint(lo, hi))] for _ in range(n)]
+
+    def toks_lps(o):
+        c = o.outputs[0]
+        return list(c.token_ids), [float(list(d.values())[0].logprob) for d in (c.logprobs or [])]
+
+    if arm == "exact":
+        P = prompts_of(64, 1024, 1024, 0)
+        tgt, oth = P[:16], P[16:]
+        order, tpos = [], []
+        for j in range(16):  # t0, o0, o1, o2, t1, o3, ...
+            tpos.append(len(order))
+            order.append(tgt[j])
+            order += oth[3 * j:3 * j + 3]
+        for temp in (1.0, 0.0):
+            def mk(seed):
+                return SamplingParams(temperature=temp, top_k=20 if temp > 0 else -1, top_p=0.95 if temp > 0 else 1.0,
+                                      max_tokens=256, seed=seed, logprobs=0, ignore_eos=True, detokenize=False)
+            run = lambda ps, sps: [toks_lps(o) for o in llm.generate([{"prompt_token_ids": p} for p in ps], sps,
+                                                                     use_tqdm=False)]
+            sa = [mk(1000 + j) for j in range(16)]
+            A = run(tgt, sa)
+            outb = run(order, [mk(1000 + tpos.index(i)) if i in tpos else mk(1100 + i) for i in range(len(order))])
+            B = [outb[i] for i in tpos]
+            C = run(tgt, sa)
+            same = lambda X, Y: (sum(x[0] == y[0] for x, y in zip(X, Y)), sum(x[1] == y[1] for x, y in zip(X, Y)))
+            res["invariance"][f"T{temp}"] = {"A_vs_B_tokens_logprobs": "%d/16, %d/16" % same(A, B),
+                                             "A_vs_C_tokens_logprobs": "%d/16, %d/16" % same(A, C)}
+            print(json.dumps({"partial": res}), file=sys.stderr, flush=True)
+    for n, ctx in (STEP_CONFIGS[:1] if args.quick else STEP_CONFIGS):
+        prompts = [{"prompt_token_ids": p} for p in prompts_of(n, int(0.75 * ctx), int(1.25 * ctx), n * 7 + ctx)]
+
+        def gen(k):
+            sps = [SamplingParams(temperature=1.0, top_k=20, top_p=0.95, max_tokens=k, ignore_eos=True, seed=j,
+                                  detokenize=False) for j in range(n)]
+            t = time.time()
+            llm.generate(prompts, sps, use_tqdm=False)
+            return time.time() - t
+        gen(321)
+        step = (min(gen(321), gen(321)) - min(gen(65), gen(65))) / 256
+        res["speed"][f"b{n}/{ctx // 1024}K"] = {"step_ms": round(step * 1000, 3), "tok_per_s": round(n / step, 1)}
+        print(json.dumps({"partial": res}), file=sys.stderr, flush=True)
+    print("ENGINE_JSON " + json.dumps(res), flush=True)
+
+
 def run_case(args):
     """Workloads for ncu captures, run eagerly --reps times (ncu flushes caches before each captured pass):
     `gemm:<shape>:<M>[:<algo>]` one GEMM, `attn:<n>:<ctx>` one attention batch, `sweep` the 15 GEMMs of the headline
     decode step."""
+    if args.case.startswith("engine"):
+        return engine_case(args)
     import torch
     from vllm_exact import kernels as KK, paged_attn as PA
     import recipes as R
