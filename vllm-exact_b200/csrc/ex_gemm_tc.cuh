@@ -649,7 +649,18 @@ static TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int split_k, int algo, in
   p.gs = std::min(p.m_tiles, 8);
   p.chunks = (p.m_tiles + p.gs - 1) / p.gs;
   const int units = pair ? sms / 2 : sms;  // CTA pairs or CTAs resident at once (one per SM)
-  int64_t groups = split_k > 0 ? (int64_t)p.n_tiles * split_k : std::max<int64_t>(1, units / p.gs);
+  const int64_t fit = std::max<int64_t>(1, units / p.gs);  // groups resident at once
+  int64_t groups = fit;  // automatic default: the balanced (n-tile, k-step) partition over every resident group
+  if (split_k > 0) {
+    groups = (int64_t)p.n_tiles * split_k;
+  } else {
+    // Tile-aligned partition when it keeps at least 60% of the groups busy: every n-tile split into s equal K ranges
+    // (s = 1: whole tiles, no workspace). Fewer, aligned split tiles cost less in reduction and finishing than the
+    // balanced partition's ragged ones; measured on B200 it wins for the narrow layers (o_proj M=64 17.5 -> 15.2 us,
+    // qkv M=256 34.6 -> 26.6 us) and is not taken for wide ones (gate_up, lm_head), where it would not apply.
+    const int64_t s = fit / p.n_tiles;
+    if (s >= 1 && (int64_t)p.n_tiles * s * 10 >= fit * 6) groups = (int64_t)p.n_tiles * s;
+  }
   groups = std::max<int64_t>(1, std::min<int64_t>(groups, p.T));
   groups = std::min<int64_t>(groups, 2147483647 / p.gs);
   p.groups = (int)groups;
