@@ -701,12 +701,74 @@ def engine_case(args):
     print("ENGINE_JSON " + json.dumps(res), flush=True)
 
 
+def tp_case(args):
+    """Row-parallel (K-sharded) exact layers on the torchrun group: time per layer call of the NCCL path (int64 SUM
+    all-reduce + epilogue kernel) and of the fused peer-memory path (PeerEpilogue: one kernel reads the peers'
+    partials over NVLink and applies the epilogue), both captured in CUDA graphs (20 calls per graph), device time,
+    max over ranks. Both paths include the row-max all-reduce, the digitizer and the partial GEMM. Prints one JSON
+    line on rank 0. Launch: torchrun --nproc-per-node N bench.py --case tp."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from vllm_exact import kernels as KK, parallel as P
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    peer = P.PeerEpilogue(64, 4096)
+    res = {}
+    for name, Kd, N in (("o_proj", 4096, 4096), ("down", 12288, 4096)):
+        ks = Kd // world
+        w = (torch.randn(N, ks, generator=torch.Generator().manual_seed(rank)) * 0.02).bfloat16().to(dev)
+        wd = P.digitize_weight_row_sharded(w, 14)
+        for M in (1, 16, 64):
+            x = torch.randn(M, ks, generator=torch.Generator().manual_seed(M)).bfloat16().to(dev)
+            st = torch.cuda.Stream(dev)
+            KK.reserve_workspace(KK.lib().ex_linear_workspace_bytes(M, N, ks, 0, 0), dev, stream=st)
+            row = {}
+            for path in ("nccl", "peer"):
+                fn = (lambda: P.row_parallel_linear(x, *wd, 14, True)) if path == "nccl" else \
+                    (lambda: peer.linear(x, *wd, 14, True))
+                st.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(st):
+                    fn()
+                torch.cuda.synchronize(dev)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=st):
+                    for _ in range(20):
+                        fn()
+                g.replay()
+                torch.cuda.synchronize(dev)
+                dist.barrier()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(st):
+                    a.record()
+                    for _ in range(5):
+                        g.replay()
+                    b.record()
+                torch.cuda.synchronize(dev)
+                t = torch.tensor([a.elapsed_time(b) * 1000 / 100], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                row[path] = round(float(t), 2)
+                del g
+            res[f"{name}/M{M}"] = row
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    peer.close()
+    if rank == 0:
+        print(json.dumps({"case": "tp", "world": world, "us_per_layer_call": res}), flush=True)
+    dist.destroy_process_group()
+
+
 def run_case(args):
     """Workloads for ncu captures, run eagerly --reps times (ncu flushes caches before each captured pass):
     `gemm:<shape>:<M>[:<algo>]` one GEMM, `attn:<n>:<ctx>` one attention batch, `sweep` the 15 GEMMs of the headline
     decode step."""
     if args.case.startswith("engine"):
         return engine_case(args)
+    if args.case == "tp":
+        return tp_case(args)
     import torch
     from vllm_exact import kernels as KK, paged_attn as PA
     import recipes as R

@@ -147,6 +147,37 @@ int ex_linear_partial_i64(const int8_t* xh, const int8_t* xl, int64_t ldx, const
 int ex_epilogue_i64(const int64_t* tot, int64_t ldt, const int32_t* sx, const int32_t* sw, int64_t M, int64_t N,
                     void* out, int out_dtype, int64_t ldo, void* stream);
 
+/*
+ * Tensor parallelism over peer memory (no counterpart in the reference, which has no multi-GPU path; the exactness
+ * argument is kernels.py:144-146, :159-177: int64 partial totals of disjoint K slices add up to the full total).
+ *
+ * CUDA IPC: ex_ipc_get_handle exports the device allocation that contains dev_ptr (handle of EX_IPC_HANDLE_BYTES
+ * bytes) and the byte offset of dev_ptr inside it (allocators hand out pieces of larger allocations);
+ * ex_ipc_open_handle maps an allocation exported by another process on this GPU (plain peer mapping, no multicast
+ * object) and returns its base, to which the caller adds the exporter's offset; ex_ipc_close_handle unmaps a base.
+ */
+#define EX_IPC_HANDLE_BYTES 64
+int ex_ipc_get_handle(const void* dev_ptr, unsigned char* handle, uint64_t* offset);
+int ex_ipc_open_handle(const unsigned char* handle, void** base);
+int ex_ipc_close_handle(void* base);
+
+/*
+ * Fused all-reduce + epilogue of K-sharded partial totals: replaces the int64 SUM all-reduce of the partials followed
+ * by ex_epilogue_i64 for a row-parallel layer, in one kernel that reads the peers' partials over NVLink.
+ *   parts  device array of `world` pointers: the (M, N) int64 partial total (leading dimension ldt) of every rank,
+ *          this rank's at index `rank`, all readable from this GPU (e.g. mapped with ex_ipc_open_handle)
+ *   flags  device array of `world` pointers: every rank's int32 flag array of 2 * world entries, zero-filled once
+ *   ctl    this rank's two int32 control words, zero-filled once (the call's epoch lives here, on the device)
+ * Every rank signals its partial ready in every flag array, waits (bounded) for every rank's partial of this call,
+ * sums the partials (exact), applies the exact epilogue, writes its own `out`, and before the kernel completes waits
+ * (bounded) until every rank has finished reading its partial: the partial buffer may be rewritten by the next work
+ * on the stream, and the call can be captured in a CUDA graph. Calls must be made in the same order on every rank.
+ * A wait that runs out records a device error (ex_device_error).
+ */
+int ex_allreduce_epilogue_i64(const void* parts, int64_t ldt, const void* flags, int32_t* ctl, int rank, int world,
+                              const int32_t* sx, const int32_t* sw, int64_t M, int64_t N, void* out, int out_dtype,
+                              int64_t ldo, void* stream);
+
 /* Bytes of (uninitialised) partial-result workspace ex_paged_decode needs. */
 size_t ex_paged_decode_workspace_bytes(int n, int H, int D, int max_len, int split);
 

@@ -130,3 +130,173 @@ def test_config3_k_sharded_on_2_4_8_gpus():
             assert p.exitcode == 0
         for r in range(world):
             assert all(res[r].values()), (world, r, res[r])
+
+
+def _worker_peer(rank, world, port, root, q):
+    """The fused peer-memory all-reduce + epilogue (PeerEpilogue) against the NCCL path and the 1-GPU result, over
+    enough calls that both partial buffers are reused."""
+    import sys
+    for p in (root, os.path.join(root, "vllm-exact_b200"), os.path.join(root, "tests", "golden")):
+        sys.path.insert(0, p)
+    import datetime
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            device_id=dev, timeout=datetime.timedelta(seconds=60))
+    peer = None
+    try:
+        import recipes as R
+        from vllm_exact import kernels as K, parallel as P
+        peer = P.PeerEpilogue(256, 4096)
+        res = {}
+        for it, (M, N, Kd, F, tr) in enumerate([(1, 4096, 4096, 14, True), (16, 4096, 12288, 14, True),
+                                                (64, 1024, 4096, 15, False), (5, 200, 12288, 15, True),
+                                                (256, 4096, 4096, 14, True), (16, 4096, 12288, 14, True)]):
+            x, w = R.extreme_digits(M, N, Kd, seed=it)
+            x[1 % M] *= 1e-3
+            xb, wb = x.bfloat16().to(dev), w.bfloat16().to(dev)
+            ref = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            K.exact_linear(K.digitize(xb, F), K.digitize(wb, F), F, tr, out=ref)
+            ks = Kd // world
+            a, b = rank * ks, (rank + 1) * ks
+            wd = P.digitize_weight_row_sharded(wb[:, a:b].contiguous(), F)
+            y_nccl = P.row_parallel_linear(xb[:, a:b], *wd, F, tr)
+            y_peer = peer.linear(xb[:, a:b], *wd, F, tr)
+            res[it] = (bool(torch.equal(y_peer, ref)), bool(torch.equal(y_nccl, ref)))
+        # CUDA graph: one call captured (NCCL row-max all-reduce included), replayed with new inputs; the epoch lives
+        # on the device, so every replay runs a fresh round of the peer protocol
+        M, N, Kd = 16, 4096, 12288
+        ks = Kd // world
+        a, b = rank * ks, (rank + 1) * ks
+        w = (torch.randn(N, Kd, generator=torch.Generator().manual_seed(7)) * 0.02).bfloat16().to(dev)
+        wd_full = K.digitize(w, 14)
+        wd = P.digitize_weight_row_sharded(w[:, a:b].contiguous(), 14)
+        xin = torch.zeros(M, ks, dtype=torch.bfloat16, device=dev)
+        st = torch.cuda.Stream(dev)
+        K.reserve_workspace(K.lib().ex_linear_workspace_bytes(M, N, ks, 0, 0), dev, stream=st)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(st):
+            peer.linear(xin, *wd, 14, True)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            yg = peer.linear(xin, *wd, 14, True)
+        for t in range(3):
+            x = torch.randn(M, Kd, generator=torch.Generator().manual_seed(100 + t)).bfloat16().to(dev)
+            ref = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            K.exact_linear(K.digitize(x, 14), wd_full, 14, True, out=ref)
+            xin.copy_(x[:, a:b])
+            torch.cuda.synchronize(dev)
+            g.replay()
+            torch.cuda.synchronize(dev)
+            res[f"graph{t}"] = (bool(torch.equal(yg, ref)), True)
+        del g
+        torch.cuda.synchronize()
+        code = ctypes_code()
+        q.put((rank, res, code))
+    finally:
+        torch.cuda.synchronize()
+        dist.barrier()
+        if peer is not None:
+            peer.close()
+        dist.destroy_process_group()
+
+
+def ctypes_code():
+    import ctypes
+    from vllm_exact import _lib
+    c = ctypes.c_int(0)
+    _lib.lib().ex_device_error(ctypes.byref(c))
+    return c.value
+
+
+def test_peer_epilogue_two_or_more_gpus_bitexact():
+    """Row-parallel layers with the fused peer-memory all-reduce + epilogue give the 1-GPU bits (and the NCCL path's)
+    on every rank, for 2 GPUs and, where present, 4 and 8."""
+    n = torch.cuda.device_count()
+    if n < 2:
+        pytest.skip("needs 2 GPUs")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    ctx = mp.get_context("spawn")
+    for world in (w for w in (2, 4, 8) if w <= n):
+        q = ctx.Queue()
+        port = _port()
+        procs = [ctx.Process(target=_worker_peer, args=(r, world, port, root, q)) for r in range(world)]
+        for p in procs:
+            p.start()
+        res = {}
+        for _ in procs:
+            r, v, code = q.get(timeout=600)
+            res[r] = (v, code)
+        for p in procs:
+            p.join(timeout=120)
+            assert p.exitcode == 0
+        for r in range(world):
+            v, code = res[r]
+            assert code == 0, (world, r, code)
+            assert all(a and b for a, b in v.values()), (world, r, v)
+
+
+def _one_gpu_peer_args(dev, M, N, world):
+    """Device arrays for a single-GPU call of ex_allreduce_epilogue_i64: every 'rank' is this process."""
+    parts = [torch.randint(-2**40, 2**40, (M, N), dtype=torch.int64, device=dev) for _ in range(world)]
+    flags = torch.zeros(2 * world, dtype=torch.int32, device=dev)
+    ctl = torch.zeros(2, dtype=torch.int32, device=dev)
+    part_ptrs = torch.tensor([t.data_ptr() for t in parts], dtype=torch.int64, device=dev)
+    flag_ptrs = torch.tensor([flags.data_ptr()] * world, dtype=torch.int64, device=dev)
+    return parts, flags, ctl, part_ptrs, flag_ptrs
+
+
+def test_peer_epilogue_one_rank_equals_epilogue():
+    """world = 1: the fused kernel is the plain exact epilogue (bitwise vs ex_epilogue_i64)."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "vllm-exact_b200"))
+    from vllm_exact import _lib, kernels as K
+    dev = torch.device("cuda", 0)
+    M, N = 33, 1000
+    parts, flags, ctl, part_ptrs, flag_ptrs = _one_gpu_peer_args(dev, M, N, 1)
+    sx = torch.randint(10, 20, (M,), dtype=torch.int32, device=dev)
+    sw = torch.randint(15, 20, (N,), dtype=torch.int32, device=dev)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.check("ex_allreduce_epilogue_i64",
+               _lib.lib().ex_allreduce_epilogue_i64(part_ptrs.data_ptr(), N, flag_ptrs.data_ptr(), ctl.data_ptr(),
+                                                    0, 1, sx.data_ptr(), sw.data_ptr(), M, N, y.data_ptr(),
+                                                    _lib.EX_DTYPE_BF16, N, st))
+    ref = torch.empty_like(y)
+    K.exact_epilogue(parts[0], sx, sw, ref)
+    assert torch.equal(y, ref)
+    assert ctypes_code() == 0
+    assert ctl.tolist() == [1, 0] and flags.tolist() == [1, 1]  # epoch advanced on the device, both barriers passed
+
+
+def test_peer_epilogue_missing_peer_times_out_with_status():
+    """Failure detection without a GPU fault: a 'peer' that never signals (a flag nothing sets) makes the bounded
+    waits run out (about 2 s each: the ready wait, then the done wait of the last block); the kernel records
+    EX_DEVERR_WAIT_PEER (6), writes no output and the context stays usable."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "vllm-exact_b200"))
+    from vllm_exact import _lib
+    dev = torch.device("cuda", 0)
+    M, N = 4, 256
+    parts, flags, ctl, part_ptrs, flag_ptrs = _one_gpu_peer_args(dev, M, N, 2)
+    sx = torch.full((M,), 12, dtype=torch.int32, device=dev)
+    sw = torch.full((N,), 17, dtype=torch.int32, device=dev)
+    y = torch.full((M, N), 7.0, dtype=torch.float32, device=dev)
+    assert ctypes_code() == 0
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.check("ex_allreduce_epilogue_i64",
+               _lib.lib().ex_allreduce_epilogue_i64(part_ptrs.data_ptr(), N, flag_ptrs.data_ptr(), ctl.data_ptr(),
+                                                    0, 2, sx.data_ptr(), sw.data_ptr(), M, N, y.data_ptr(),
+                                                    _lib.EX_DTYPE_F32, N, st))
+    assert ctypes_code() == 6
+    assert bool((y == 7.0).all())  # nothing written
+    z = torch.ones(8, device=dev) * 3  # the context still works
+    assert float(z.sum()) == 24.0

@@ -3,10 +3,12 @@
 // The whole library is one translation unit (this file includes the kernel headers) so that every kernel shares the
 // single device error word g_ex_dev_error. Every entry point validates its arguments before launching anything,
 // never allocates device memory and never synchronizes the host.
+#include <cstring>
 #include <mutex>
 #include <string>
 
 #include "ex_common.cuh"
+#include "ex_tp_fused.cuh"
 #include "ex_digitize.cuh"
 #include "ex_gemm_simt.cuh"
 #include "ex_gemm_tc.cuh"
@@ -360,6 +362,69 @@ int ex_epilogue_i64(const int64_t* tot, int64_t ldt, const int32_t* sx, const in
     ex::k_epilogue_i64<EX_DTYPE_BF16><<<blocks, threads, 0, st>>>(t, ldt, sx, sw, (int)M, (int)N, out, ldo);
   else
     ex::k_epilogue_i64<EX_DTYPE_F16><<<blocks, threads, 0, st>>>(t, ldt, sx, sw, (int)M, (int)N, out, ldo);
+  return cuda_status(cudaGetLastError());
+}
+
+int ex_ipc_get_handle(const void* dev_ptr, unsigned char* handle, uint64_t* offset) {
+  if (!dev_ptr || !handle || !offset) return EX_ERR_ARG;
+  typedef CUresult (*PFN_range)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static PFN_range range_fn = nullptr;
+  if (!range_fn) {
+    void* fp = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &fp, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return EX_ERR_UNSUPPORTED;
+    range_fn = reinterpret_cast<PFN_range>(fp);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range_fn(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS) return EX_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_status(e);
+  static_assert(sizeof(h) == EX_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = (uint64_t)(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
+  return EX_OK;
+}
+
+int ex_ipc_open_handle(const unsigned char* handle, void** base) {
+  if (!handle || !base) return EX_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int ex_ipc_close_handle(void* base) {
+  if (!base) return EX_ERR_ARG;
+  return cuda_status(cudaIpcCloseMemHandle(base));
+}
+
+int ex_allreduce_epilogue_i64(const void* parts, int64_t ldt, const void* flags, int32_t* ctl, int rank, int world,
+                              const int32_t* sx, const int32_t* sw, int64_t M, int64_t N, void* out, int out_dtype,
+                              int64_t ldo, void* stream) {
+  if (M < 0 || N < 0 || M > INT32_MAX || N > INT32_MAX) return EX_ERR_ARG;
+  if (world < 1 || world > 64 || rank < 0 || rank >= world) return EX_ERR_ARG;
+  if (!dtype_ok(out_dtype)) return EX_ERR_DTYPE;
+  if (!parts || !flags || !ctl || !sx || !sw || !out || ldt < N || ldo < N) return EX_ERR_ARG;
+  // every rank takes part in every call, also for an empty output (one block then only runs the barriers)
+  const int64_t total = M * N;
+  // one output per thread at decode sizes: every remote load of a thread is an NVLink round trip, so spread them
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(total, ex::TPF_THREADS), 4 * (int64_t)num_sms()));
+  cudaStream_t st = (cudaStream_t)stream;
+  const long long* const* pp = reinterpret_cast<const long long* const*>(parts);
+  int* const* fp = reinterpret_cast<int* const*>(flags);
+#define EX_TPF_LAUNCH(OD)                                                                                      \
+  ex::k_allreduce_epilogue_i64<OD><<<blocks, ex::TPF_THREADS, 0, st>>>(pp, ldt, fp, ctl, rank, world, sx, sw,   \
+                                                                        (int)M, (int)N, out, ldo)
+  if (out_dtype == EX_DTYPE_F32)
+    EX_TPF_LAUNCH(EX_DTYPE_F32);
+  else if (out_dtype == EX_DTYPE_BF16)
+    EX_TPF_LAUNCH(EX_DTYPE_BF16);
+  else
+    EX_TPF_LAUNCH(EX_DTYPE_F16);
+#undef EX_TPF_LAUNCH
   return cuda_status(cudaGetLastError());
 }
 

@@ -28,6 +28,7 @@ enum {
   EX_DEVERR_WAIT_MMA = 3,      // the epilogue gave up waiting for the accumulator
   EX_DEVERR_WAIT_TMEM = 4,     // the MMA warp gave up waiting for the epilogue to release TMEM
   EX_DEVERR_TMEM_ALLOC = 5,    // TMEM allocation returned an unexpected address
+  EX_DEVERR_WAIT_PEER = 6,     // a rank of the fused tensor-parallel epilogue gave up waiting for a peer's partial
 };
 
 __device__ __forceinline__ void ex_set_error(int code) { atomicCAS(&g_ex_dev_error, 0, code); }

@@ -11,6 +11,7 @@ LIB_PATH = Path(os.environ.get("VLLM_EXACT_B200_LIB", Path(__file__).with_name("
 
 EX_OK, EX_ERR_ARG, EX_ERR_ALIGN, EX_ERR_WORKSPACE, EX_ERR_DTYPE, EX_ERR_UNSUPPORTED, EX_ERR_CUDA, EX_ERR_DEVICE = range(8)
 EX_DTYPE_F32, EX_DTYPE_BF16, EX_DTYPE_F16 = 0, 1, 2
+EX_IPC_HANDLE_BYTES = 64
 EX_ALGO_AUTO, EX_ALGO_SIMT, EX_ALGO_TC_I8, EX_ALGO_TC_BF16, EX_ALGO_TC_I8_PAIR = 0, 1, 2, 3, 4
 
 c_i64, c_i32, c_vp, c_sz, c_f32 = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_float
@@ -33,6 +34,11 @@ SIGNATURES = {
     "ex_linear_partial_i64": (c_i32, [c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i32,
                                       c_i32, c_vp, c_i64, c_vp, c_sz, c_i32, c_i32, c_vp]),
     "ex_epilogue_i64": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_i64, c_vp]),
+    "ex_ipc_get_handle": (c_i32, [c_vp, c_vp, ctypes.POINTER(ctypes.c_uint64)]),
+    "ex_ipc_open_handle": (c_i32, [c_vp, ctypes.POINTER(c_vp)]),
+    "ex_ipc_close_handle": (c_i32, [c_vp]),
+    "ex_allreduce_epilogue_i64": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_i32, c_i32, c_vp, c_vp, c_i64, c_i64, c_vp, c_i32,
+                                          c_i64, c_vp]),
     "ex_paged_decode_workspace_bytes": (c_sz, [c_i32, c_i32, c_i32, c_i32, c_i32]),
     "ex_paged_decode": (c_i32, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_i32,
                                 c_i32, c_i32, c_i32, c_i32, c_f32, c_i32, c_i32, c_vp, c_i64, c_i64, c_i32, c_vp, c_sz,

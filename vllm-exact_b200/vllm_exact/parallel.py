@@ -14,15 +14,20 @@ The reference runs on one GPU only (README.md:95). Sharding the exact layer acro
     5. every rank applies the scaling epilogue.
   Steps 1-2 also run once for the weights at load time (the rows of a weight matrix are K-sharded too).
 
-The collectives are torch.distributed calls on the tensor-parallel group (NCCL over NVLink on GPUs). The compute
+The collectives are torch.distributed calls on the tensor-parallel group (NCCL over NVLink on GPUs). PeerEpilogue
+fuses steps 4 and 5 into one kernel that reads the other ranks' partial totals over NVLink (CUDA IPC mappings) and
+applies the epilogue, without NCCL on the data path. The compute
 steps go through an `ops` object; the product uses the sm_100a library (CudaOps). Tests can pass another `ops` to
 exercise the collective logic on CPU ranks (gloo), the way a fake device layer is used in host tests.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from . import kernels as K
 from ._lib import check, lib
 
@@ -114,3 +119,89 @@ def row_parallel_linear(x: torch.Tensor, wh, wl, cw, sw, F: int, trunc: bool, gr
     dist.all_reduce(tot, op=dist.ReduceOp.SUM, group=g)
     y = ops.epilogue(tot, xd[3], sw, out_dtype or x.dtype)
     return y.reshape(*shp[:-1], wh.shape[0])
+
+
+class PeerEpilogue:
+    """Fused all-reduce + exact epilogue of K-sharded partial totals over peer memory (ex_allreduce_epilogue_i64), in
+    place of the int64 NCCL all-reduce and the separate epilogue of row_parallel_linear. One object per process group
+    and largest output (max_rows x max_cols): every rank owns one partial buffer, one flag array (2 x world int32) and
+    two control words (the call epoch, kept on the device, so calls can be captured in CUDA graphs); the buffers are
+    shared with the other ranks through CUDA IPC handles exchanged once with all_gather_object (plain peer mappings,
+    no multicast objects). Calls must be issued in the same order on every rank of the group."""
+
+    def __init__(self, max_rows: int, max_cols: int, group=None, device=None):
+        g = group if group is not None else _default_group()
+        self.group = g
+        self.rank, self.world = dist.get_rank(g), dist.get_world_size(g)
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.device = dev
+        self.capacity = max_rows * max_cols
+        self.part = torch.empty(self.capacity, dtype=torch.int64, device=dev)
+        self.flags = torch.zeros(2 * self.world, dtype=torch.int32, device=dev)
+        self.ctl = torch.zeros(2, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        mine = [self._handle(t) for t in (self.part, self.flags)]
+        every = [None] * self.world
+        dist.all_gather_object(every, mine, group=g)
+        self._opened = []
+        self._bases = {}  # exported allocation handle -> mapped base (tensors may share one allocation)
+        ptrs = []  # ptrs[p] = (partial, flags) device addresses of rank p, as seen from this GPU
+        for p, hs in enumerate(every):
+            if p == self.rank:
+                ptrs.append([self.part.data_ptr(), self.flags.data_ptr()])
+            else:
+                ptrs.append([self._open(h) + off for h, off in hs])
+        self.part_ptrs = torch.tensor([ptrs[p][0] for p in range(self.world)], dtype=torch.int64, device=dev)
+        self.flag_ptrs = torch.tensor([ptrs[p][1] for p in range(self.world)], dtype=torch.int64, device=dev)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=g)  # every rank has mapped every buffer before the first call
+
+    def _handle(self, t: torch.Tensor):
+        """(handle of the allocation holding t, byte offset of t inside it)."""
+        buf = (ctypes.c_ubyte * _lib.EX_IPC_HANDLE_BYTES)()
+        off = ctypes.c_uint64(0)
+        with torch.cuda.device(self.device):
+            check("ex_ipc_get_handle", lib().ex_ipc_get_handle(t.data_ptr(), buf, ctypes.byref(off)))
+        return bytes(buf), off.value
+
+    def _open(self, h: bytes) -> int:
+        """Base address of another rank's exported allocation, mapped once per allocation."""
+        if h not in self._bases:
+            buf = (ctypes.c_ubyte * _lib.EX_IPC_HANDLE_BYTES).from_buffer_copy(h)
+            ptr = ctypes.c_void_p()
+            with torch.cuda.device(self.device):
+                check("ex_ipc_open_handle", lib().ex_ipc_open_handle(buf, ctypes.byref(ptr)))
+            self._opened.append(ptr.value)
+            self._bases[h] = ptr.value
+        return self._bases[h]
+
+    def close(self) -> None:
+        """Unmap the peers' buffers (after the last call has completed on every rank)."""
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                lib().ex_ipc_close_handle(p)
+        self._opened = []
+        self._bases = {}
+
+    def linear(self, x: torch.Tensor, wh, wl, cw, sw, F: int, trunc: bool, out_dtype=None) -> torch.Tensor:
+        """row_parallel_linear with the partial total written into this rank's shared buffer and the all-reduce and
+        epilogue fused over peer memory. Same arguments and bitwise the same result."""
+        shp = x.shape
+        x2 = x.reshape(-1, shp[-1])
+        if x2.stride(-1) != 1:
+            x2 = x2.contiguous()
+        M, N = x2.shape[0], wh.shape[0]
+        if M * N > self.capacity:
+            raise ValueError(f"PeerEpilogue holds {self.capacity} outputs, the call needs {M * N}")
+        amax = global_row_absmax(x2, self.group, CudaOps)
+        xd = CudaOps.digitize_given(x2, F, amax)
+        part = self.part[: M * N].view(M, N)
+        K.exact_linear_partial_i64(xd, (wh, wl, cw, sw), F, trunc, out=part)
+        y = torch.empty(M, N, dtype=out_dtype or x.dtype, device=x2.device)
+        with torch.cuda.device(x2.device):
+            check("ex_allreduce_epilogue_i64",
+                  lib().ex_allreduce_epilogue_i64(self.part_ptrs.data_ptr(), N, self.flag_ptrs.data_ptr(),
+                                                  self.ctl.data_ptr(), self.rank, self.world, xd[3].data_ptr(),
+                                                  sw.data_ptr(), M, N, y.data_ptr(), K._DT[y.dtype], y.stride(0),
+                                                  K._stream(x2.device)))
+        return y.reshape(*shp[:-1], N)
