@@ -201,6 +201,22 @@ int ex_paged_decode(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cac
                     void* out, int64_t so_t, int64_t so_h, int out_dtype, void* workspace, size_t workspace_bytes,
                     void* stream);
 
+/*
+ * ex_paged_decode for the decode requests of a mixed prefill + decode step, without a host sync.
+ * Replaces the host-side count in the patched FlashAttentionImpl.forward (src/vllm_exact/paged_attn.py:153-159:
+ * ql = query_start_loc[1:] - query_start_loc[:-1]; nd = cumprod(ql == 1).sum(); paged_decode(..., nd)).
+ * query_start_loc: int32 device array of at least n + 1 entries (n = number of requests described). Request b < n is
+ * computed, exactly as by ex_paged_decode, iff query_start_loc[i + 1] - query_start_loc[i] == 1 for every i <= b;
+ * the rows of `out` of every other request are left untouched. The count is made on the device, so the call can be
+ * captured in a CUDA graph. query_start_loc == NULL: every request b < n is computed (ex_paged_decode).
+ */
+int ex_paged_decode_leading(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cache, const void* v_cache,
+                            int64_t s_block, int64_t s_page, int64_t s_head, int64_t num_blocks,
+                            const int32_t* block_table, int64_t sbt, const int32_t* seq_lens,
+                            const int32_t* query_start_loc, int n, int H, int KV, int D, int BS, float scale,
+                            int max_len, int split, void* out, int64_t so_t, int64_t so_h, int out_dtype,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -162,3 +162,11 @@ def paged_decode(q: np.ndarray, key_cache: np.ndarray, value_cache: np.ndarray, 
             p = np.exp(sc.astype(np.float64)).astype(np.float32)
             out[b, h] = (p / p.sum()) @ v[:, h // G] if L else np.nan
     return out
+
+
+def leading_decodes(query_start_loc: np.ndarray) -> int:
+    """Number of leading requests of a mixed prefill + decode step whose query length is 1, i.e. the requests the
+    patched attention decodes (reference paged_attn.py:153-159: ql = qsl[1:] - qsl[:-1]; nd = cumprod(ql == 1).sum())."""
+    qsl = np.asarray(query_start_loc, dtype=np.int64)
+    ql = qsl[1:] - qsl[:-1]
+    return int(np.cumprod((ql == 1).astype(np.int64)).sum())

@@ -67,6 +67,14 @@ def check_plugin():
     bias = torch.randn(1024, device=dev).bfloat16()
     yb = m.apply(layer, x.to(dev), bias)
     out["bias_ok"] = bool(torch.equal(yb, y.reshape(8, 1024) + bias))
+    # optional release of the bf16 weight after digitization: apply() gives the same bits without it
+    plugin.DROP_BF16_WEIGHT = True
+    layer2 = torch.nn.Module()
+    layer2.weight = torch.nn.Parameter(w.to(dev), requires_grad=False)
+    m.process_weights_after_loading(layer2)
+    plugin.DROP_BF16_WEIGHT = False
+    out["dropped_weight_shape"] = list(layer2.weight.shape)
+    out["dropped_same_bits"] = bool(torch.equal(m.apply(layer2, x.to(dev).view(2, 4, 1024)), y))
     from vllm.model_executor.layers.vocab_parallel_embedding import ParallelLMHead
     lm = cfg.get_quant_method(ParallelLMHead.__new__(ParallelLMHead), "lm_head")
     out["lm_head_method"] = type(lm).__name__
@@ -89,6 +97,22 @@ def check_plugin():
     f = lambda t: t.detach().cpu().float().numpy()
     o_ref = O.paged_decode(f(q), f(kc), f(vc), bt.numpy(), sl.numpy(), D ** -0.5, n)
     out["patch_max_err"] = float(np.abs(f(output[:n].view(n, H, D)) - o_ref).max())
+    # mixed prefill + decode step: vLLM's own forward (stubbed here: it fills the output with 3.0) runs first, then
+    # the leading one-token requests (3 of ql = 1,1,1,4,1,2) are overwritten by the kernel without a host sync
+    fa.FlashAttentionImpl.forward = lambda self, layer, query, key, value, kv_cache, md, output, *a: output.fill_(3.0)
+    P.install()
+    ql = [1, 1, 1, 4, 1, 2]
+    qsl = torch.tensor([0] + list(np.cumsum(ql)), dtype=torch.int32, device=dev)
+    meta.max_query_len, meta.num_actual_tokens, meta.query_start_loc = 4, int(qsl[-1]), qsl
+    T = int(qsl[-1])
+    qm = torch.randn(T, H, D, generator=torch.Generator().manual_seed(3)).bfloat16().to(dev)
+    qm[:n] = qd
+    outm = torch.full((T, H * D), 7.0, device=dev, dtype=torch.bfloat16)
+    fa.FlashAttentionImpl.forward(impl, None, qm, None, None, cache, meta, outm)
+    nd = O.leading_decodes(qsl.cpu().numpy())
+    out["mixed_nd"] = nd
+    out["mixed_decodes_match"] = bool(torch.equal(outm[:nd].view(nd, H, D), ref[:nd]))
+    out["mixed_rest_from_vllm"] = bool((outm[nd:] == 3.0).all())
     return out
 
 

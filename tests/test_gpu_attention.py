@@ -120,3 +120,60 @@ def test_zero_and_short_lengths(P):
     P.paged_decode(q, kc, vc, bt, sl, 0.088, o, 4)
     ref = _oracle(q, kc, vc, bt, sl, 0.088, 4)
     assert np.abs(o.cpu().numpy() - ref).max() < TOL
+
+
+MIXED_QL = [[1] * 8, [1, 1, 1, 4, 1, 2, 1, 1], [3, 1, 1, 1, 1, 1, 1, 1], [1, 1, 0, 0, 0, 0, 0, 0],
+            [1, 1, 1, 1, 1, 1, 1, 2], [2] * 8]
+
+
+def _qsl(ql):
+    return torch.tensor(np.concatenate([[0], np.cumsum(ql)]), dtype=torch.int32, device=DEV)
+
+
+@pytest.mark.parametrize("H,KV,D", [(32, 8, 128), (16, 4, 256)])  # TMA page-gather kernel, cp.async kernel
+@pytest.mark.parametrize("ql", MIXED_QL)
+def test_mixed_step_leading_decodes(P, H, KV, D, ql):
+    """Mixed prefill + decode step (reference paged_attn.py:153-159) without a host sync: given query_start_loc, the
+    kernel computes exactly the leading requests of query length 1 (count from the oracle's restatement of the
+    reference rule), bitwise equal to a plain decode of them, and leaves every other output row untouched."""
+    B, BS = len(ql), 16
+    q, kv, bt, sl = _case(B, 700, BS, H, KV, D, jitter=True)
+    kc, vc = R.kv_views(kv, D)
+    qsl = _qsl(ql)
+    nd = O.leading_decodes(qsl.cpu().numpy())
+    full = torch.empty(B, H, D, device=DEV, dtype=torch.bfloat16)
+    P.paged_decode(q, kc, vc, bt, sl, 0.1, full, B)
+    o = torch.full((B, H, D), 7.0, device=DEV, dtype=torch.bfloat16)
+    P.paged_decode(q, kc, vc, bt, sl, 0.1, o, B, query_start_loc=qsl)
+    assert torch.equal(o[:nd], full[:nd])
+    assert bool((o[nd:] == 7.0).all())
+
+
+def test_mixed_step_graph_replay_follows_query_start_loc(P):
+    """The mixed-step call captured once in a CUDA graph: replays with different query_start_loc contents decode
+    exactly the leading one-token requests of each (the count is made on the device at every replay)."""
+    H, KV, D, BS, B = 32, 8, 128, 16, 8
+    q, kv, bt, sl = _case(B, 700, BS, H, KV, D, jitter=True)
+    kc, vc = R.kv_views(kv, D)
+    full = torch.empty(B, H, D, device=DEV, dtype=torch.bfloat16)
+    P.paged_decode(q, kc, vc, bt, sl, 0.1, full, B)
+    qsl = _qsl(MIXED_QL[0])
+    o = torch.empty(B, H, D, device=DEV, dtype=torch.bfloat16)
+    ws = torch.empty(P.workspace_bytes(B, H, D), dtype=torch.uint8, device=DEV)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        P.paged_decode(q, kc, vc, bt, sl, 0.1, o, B, workspace=ws, query_start_loc=qsl)  # warm-up outside capture
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        P.paged_decode(q, kc, vc, bt, sl, 0.1, o, B, workspace=ws, query_start_loc=qsl)
+    for ql in MIXED_QL[1:] + MIXED_QL[:1]:
+        qsl.copy_(_qsl(ql))
+        o.fill_(7.0)
+        g.replay()
+        torch.cuda.synchronize()
+        nd = O.leading_decodes(qsl.cpu().numpy())
+        assert torch.equal(o[:nd], full[:nd]), ql
+        assert bool((o[nd:] == 7.0).all()), ql
+    del g

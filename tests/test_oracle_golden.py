@@ -112,3 +112,35 @@ def test_k_split_is_exact():
         parts = parts + O.exact_linear_i64([xd[0][:, s], xd[1][:, s], xd[2], xd[3]],
                                            [wd[0][:, s], wd[1][:, s], wd[2], wd[3]], 14, True)
     assert np.array_equal(whole, parts)
+
+
+def _reference_nd(qsl: torch.Tensor) -> int:
+    """The reference's own expression for the decode count of a mixed step (paged_attn.py:155-157)."""
+    ql = qsl[1:] - qsl[:-1]
+    return int(torch.cumprod((ql == 1).to(torch.int32), 0).sum().item())
+
+
+def test_leading_decodes_rule():
+    """oracle.leading_decodes equals the reference's expression, and the per-request rule the attention kernels apply
+    on the device (request b decoded iff every query length up to b is 1) selects exactly requests [0, nd)."""
+    rng = np.random.default_rng(0)
+    cases = [[1] * 8, [1, 1, 1, 4, 1, 2], [3, 1, 1], [1, 1, 0, 0], [], [1], [2], [1, 1, 1, 1, 2]]
+    cases += [list(rng.choice([0, 1, 1, 1, 2, 5], size=int(rng.integers(0, 13)))) for _ in range(300)]
+    for ql in cases:
+        qsl = torch.tensor([0] + list(np.cumsum(ql, dtype=np.int64)), dtype=torch.int32)
+        nd = O.leading_decodes(qsl.numpy())
+        assert nd == _reference_nd(qsl), ql
+        q = qsl.numpy()
+        device_rule = [all(q[i + 1] - q[i] == 1 for i in range(b + 1)) for b in range(len(ql))]
+        assert device_rule == [b < nd for b in range(len(ql))], ql
+
+
+def test_mixed_step_request_bound():
+    """Host side of the patched mixed step: the request count handed to the kernel comes from tensor shapes only."""
+    from vllm_exact import paged_attn as P
+    qsl = torch.zeros(7, dtype=torch.int32)
+    assert P.mixed_step_requests(qsl, torch.zeros(6, 4), torch.zeros(6), torch.zeros(10, 2, 2)) == 6
+    assert P.mixed_step_requests(qsl, torch.zeros(4, 4), torch.zeros(6), torch.zeros(10, 2, 2)) == 4
+    assert P.mixed_step_requests(qsl, torch.zeros(6, 4), torch.zeros(6), torch.zeros(3, 2, 2)) == 3
+    assert P.mixed_step_requests(torch.zeros(1, dtype=torch.int32), torch.zeros(6, 4), torch.zeros(6),
+                                 torch.zeros(3, 2, 2)) == 0

@@ -52,5 +52,8 @@ def test_plugin_methods_and_attention_patch_on_gpu():
     assert r["shape"] == [2, 4, 1024]
     assert r["config1_sha_ok"] is True
     assert r["bias_ok"] is True
+    assert r["dropped_weight_shape"] == [0, 1024] and r["dropped_same_bits"] is True  # DROP_BF16_WEIGHT
     assert r["patch_matches_kernel"] is True and r["padding_untouched"] is True
     assert r["patch_max_err"] < 1e-3
+    assert r["mixed_nd"] == 3  # mixed step: leading decodes found on the device, the rest left to vLLM's forward
+    assert r["mixed_decodes_match"] is True and r["mixed_rest_from_vllm"] is True

@@ -203,16 +203,19 @@ bool encode_kv_map(CUtensorMap* map, const void* base, int D, int KV, int BS, in
 }
 
 int launch_merge(const float* ws_m, const float* ws_l, const float* ws_acc, void* out, int64_t so_t, int64_t so_h,
-                 int n, int H, int NS, int D, int out_dtype, cudaStream_t st) {
+                 int n, int H, int NS, int D, int out_dtype, const int32_t* qsl, cudaStream_t st) {
   const int mthreads = std::min(D, 256);
   const dim3 mg(n * H), mb(mthreads);
   cudaError_t e;
   if (out_dtype == EX_DTYPE_BF16)
-    e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_BF16>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
+    e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_BF16>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D,
+                      qsl);
   else if (out_dtype == EX_DTYPE_F16)
-    e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_F16>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
+    e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_F16>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D,
+                      qsl);
   else
-    e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_F32>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D);
+    e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_F32>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D,
+                      qsl);
   if (e != cudaSuccess) return cuda_status(e);
   return cuda_status(cudaGetLastError());
 }
@@ -441,6 +444,17 @@ int ex_paged_decode(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cac
                     const int32_t* seq_lens, int n, int H, int KV, int D, int BS, float scale, int max_len, int split,
                     void* out, int64_t so_t, int64_t so_h, int out_dtype, void* workspace, size_t workspace_bytes,
                     void* stream) {
+  return ex_paged_decode_leading(q, sq_t, sq_h, k_cache, v_cache, s_block, s_page, s_head, num_blocks, block_table,
+                                 sbt, seq_lens, nullptr, n, H, KV, D, BS, scale, max_len, split, out, so_t, so_h,
+                                 out_dtype, workspace, workspace_bytes, stream);
+}
+
+int ex_paged_decode_leading(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cache, const void* v_cache,
+                            int64_t s_block, int64_t s_page, int64_t s_head, int64_t num_blocks,
+                            const int32_t* block_table, int64_t sbt, const int32_t* seq_lens,
+                            const int32_t* query_start_loc, int n, int H, int KV, int D, int BS, float scale,
+                            int max_len, int split, void* out, int64_t so_t, int64_t so_h, int out_dtype,
+                            void* workspace, size_t workspace_bytes, void* stream) {
   if (n < 0 || H <= 0 || KV <= 0 || H % KV != 0 || BS <= 0 || split <= 0 || max_len < 0) return EX_ERR_ARG;
   const int G = H / KV;
   if (G > 16) return EX_ERR_UNSUPPORTED;
@@ -453,6 +467,7 @@ int ex_paged_decode(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cac
       s_block % 8 != 0 || s_page % 8 != 0 || s_head % 8 != 0)
     return EX_ERR_ALIGN;
   if (reinterpret_cast<uintptr_t>(q) % 4 != 0 || sq_t % 2 != 0 || sq_h % 2 != 0) return EX_ERR_ALIGN;
+  if (reinterpret_cast<uintptr_t>(query_start_loc) % 4 != 0) return EX_ERR_ALIGN;
   const size_t need = ex_paged_decode_workspace_bytes(n, H, D, max_len, split);
   if (!workspace || workspace_bytes < need) return EX_ERR_WORKSPACE;
   if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return EX_ERR_ALIGN;
@@ -481,13 +496,13 @@ int ex_paged_decode(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cac
     e = cudaFuncSetAttribute(ex::k_paged_tma<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);            \
     if (e == cudaSuccess)                                                                                        \
       e = ex_launch_pdl(ex::k_paged_tma<DD>, grid, blk, smem, st, mk, mv, qp, sq_t, sq_h, block_table, sbt,      \
-                        seq_lens, H, G, BS, scale, split, NS, ws_m, ws_l, ws_acc);                               \
+                        seq_lens, query_start_loc, H, G, BS, scale, split, NS, ws_m, ws_l, ws_acc);              \
   }
       if (D == 64) EX_PT_LAUNCH(64)
       else EX_PT_LAUNCH(128)
 #undef EX_PT_LAUNCH
       if (e != cudaSuccess) return cuda_status(e);
-      return launch_merge(ws_m, ws_l, ws_acc, out, so_t, so_h, n, H, NS, D, out_dtype, st);
+      return launch_merge(ws_m, ws_l, ws_acc, out, so_t, so_h, n, H, NS, D, out_dtype, query_start_loc, st);
     }
   }
 #define EX_PD_LAUNCH(DD)                                                                                         \
@@ -496,8 +511,8 @@ int ex_paged_decode(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cac
     e = cudaFuncSetAttribute(ex::k_paged_partial<DD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);        \
     if (e == cudaSuccess)                                                                                        \
       e = ex_launch_pdl(ex::k_paged_partial<DD>, grid, dim3(ex::PD_THREADS), smem, st, qp, sq_t, sq_h, kp, vp,   \
-                        s_block, s_page, s_head, block_table, sbt, seq_lens, H, G, BS, scale, split, NS, ws_m,   \
-                        ws_l, ws_acc);                                                                           \
+                        s_block, s_page, s_head, block_table, sbt, seq_lens, query_start_loc, H, G, BS, scale,   \
+                        split, NS, ws_m, ws_l, ws_acc);                                                          \
   }
   if (D == 64) EX_PD_LAUNCH(64)
   else if (D == 128) EX_PD_LAUNCH(128)
@@ -505,7 +520,7 @@ int ex_paged_decode(const void* q, int64_t sq_t, int64_t sq_h, const void* k_cac
 #undef EX_PD_LAUNCH
   if (e != cudaSuccess) return cuda_status(e);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e);
-  return launch_merge(ws_m, ws_l, ws_acc, out, so_t, so_h, n, H, NS, D, out_dtype, st);
+  return launch_merge(ws_m, ws_l, ws_acc, out, so_t, so_h, n, H, NS, D, out_dtype, query_start_loc, st);
 }
 
 }  // extern "C"

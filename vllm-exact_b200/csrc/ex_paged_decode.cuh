@@ -72,17 +72,29 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Mixed prefill + decode steps: the reference counts on the host the leading requests whose query length is 1
+// (paged_attn.py:153-159, nd = cumprod(ql == 1).sum(), a host sync) and decodes requests [0, nd). Here every block
+// evaluates the same rule on the device: request b is decoded iff qsl[i + 1] - qsl[i] == 1 for every i <= b (qsl =
+// query_start_loc, at least b + 2 entries). Block-wide vote: every thread of the block must call it.
+__device__ __forceinline__ bool pd_in_leading_decodes(const int32_t* __restrict__ qsl, int b) {
+  int ok = 1;
+  for (int i = threadIdx.x; i <= b; i += blockDim.x) ok &= (qsl[i + 1] - qsl[i] == 1) ? 1 : 0;
+  return __syncthreads_and(ok) != 0;
+}
+
 template <int D>
 __global__ void __launch_bounds__(PD_THREADS, 2)
     k_paged_partial(const __nv_bfloat16* __restrict__ q, int64_t sq_t, int64_t sq_h,
                     const __nv_bfloat16* __restrict__ kc, const __nv_bfloat16* __restrict__ vc, int64_t s_block,
                     int64_t s_page, int64_t s_head, const int32_t* __restrict__ bt, int64_t sbt,
-                    const int32_t* __restrict__ seq_lens, int H, int G, int BS, float scale, int split, int NS,
-                    float* __restrict__ ws_m, float* __restrict__ ws_l, float* __restrict__ ws_acc) {
+                    const int32_t* __restrict__ seq_lens, const int32_t* __restrict__ qsl, int H, int G, int BS,
+                    float scale, int split, int NS, float* __restrict__ ws_m, float* __restrict__ ws_l,
+                    float* __restrict__ ws_acc) {
   using C = PdCfg<D>;
   extern __shared__ __align__(1024) uint8_t pd_smem[];
   pdl_launch_dependents();  // the merge kernel's prologue may start; it waits for this grid before reading
   pdl_wait();               // query / cache / block table come from earlier kernels
+  if (qsl != nullptr && !pd_in_leading_decodes(qsl, blockIdx.x)) return;  // not a leading decode: nothing to do
   const int b = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int kg = warp / C::DSPLIT, dh = warp % C::DSPLIT;
@@ -309,11 +321,12 @@ __global__ void __launch_bounds__(PD_THREADS, 2)
 template <int OUT_DTYPE>
 __global__ void k_paged_merge(const float* __restrict__ ws_m, const float* __restrict__ ws_l,
                               const float* __restrict__ ws_acc, void* out, int64_t so_t, int64_t so_h, int H, int NS,
-                              int D) {
+                              int D, const int32_t* __restrict__ qsl) {
   pdl_launch_dependents();
   pdl_wait();
   const int bh = blockIdx.x;
   const int b = bh / H, h = bh % H;
+  if (qsl != nullptr && !pd_in_leading_decodes(qsl, b)) return;  // row b belongs to a prefill: left untouched
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float m = -INFINITY, l = 0.0f, acc = 0.0f;
     for (int s = 0; s < NS; ++s) {

@@ -57,8 +57,9 @@ template <int D>
 __global__ void __launch_bounds__(PT_THREADS, 2)
     k_paged_tma(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                 const __nv_bfloat16* __restrict__ q, int64_t sq_t, int64_t sq_h, const int32_t* __restrict__ bt,
-                int64_t sbt, const int32_t* __restrict__ seq_lens, int H, int G, int BS, float scale, int split,
-                int NS, float* __restrict__ ws_m, float* __restrict__ ws_l, float* __restrict__ ws_acc) {
+                int64_t sbt, const int32_t* __restrict__ seq_lens, const int32_t* __restrict__ qsl, int H, int G,
+                int BS, float scale, int split, int NS, float* __restrict__ ws_m, float* __restrict__ ws_l,
+                float* __restrict__ ws_acc) {
   using C = PtCfg<D>;
   extern __shared__ uint8_t pt_smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(pt_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -69,6 +70,7 @@ __global__ void __launch_bounds__(PT_THREADS, 2)
   const int b = blockIdx.x, g = blockIdx.y, s = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   pdl_wait();
+  if (qsl != nullptr && !pd_in_leading_decodes(qsl, b)) return;  // not a leading decode (mixed step): nothing to do
   const int L = seq_lens[b];
   const int start = s * split;
   const int end = min(start + split, L);

@@ -43,6 +43,9 @@ SIGNATURES = {
     "ex_paged_decode": (c_i32, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_i32,
                                 c_i32, c_i32, c_i32, c_i32, c_f32, c_i32, c_i32, c_vp, c_i64, c_i64, c_i32, c_vp, c_sz,
                                 c_vp]),
+    "ex_paged_decode_leading": (c_i32, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp,
+                                        c_vp, c_i32, c_i32, c_i32, c_i32, c_i32, c_f32, c_i32, c_i32, c_vp, c_i64, c_i64,
+                                        c_i32, c_vp, c_sz, c_vp]),
 }
 
 _LIB = None

@@ -33,14 +33,26 @@ def workspace_bytes(n: int, H: int, D: int, max_len: int | None = None, split: i
 
 
 def paged_decode(query, key_cache, value_cache, block_table, seq_lens, scale, out, n, max_seq_len=None, blk=None,
-                 warps=None, stages=None, split=None, workspace=None):
+                 warps=None, stages=None, split=None, workspace=None, query_start_loc=None):
     """query (>=n, H, D) bf16; key_cache / value_cache (num_blocks, block_size, KV, D) bf16 views (any strides with a
     contiguous last dimension); block_table (>=n, pages) int32; seq_lens (>=n,) int32; out (>=n, H, D).
     Computes the first n requests only. `max_seq_len`, `blk`, `warps` and `stages` are accepted for signature
-    compatibility with the reference; the segment count comes from MAX_LEN as in the reference."""
+    compatibility with the reference; the segment count comes from MAX_LEN as in the reference.
+
+    query_start_loc (int32, >= n + 1 entries; mixed prefill + decode steps): of the first n requests, compute only
+    the leading run whose query length is 1 (the requests [0, nd) of reference paged_attn.py:153-159) and leave the
+    other rows of `out` untouched. The run is found on the device, so there is no host sync."""
     if n <= 0:
         return out
-    for t in (query, key_cache, value_cache, block_table, seq_lens, out):
+    tensors = (query, key_cache, value_cache, block_table, seq_lens, out)
+    if query_start_loc is not None:
+        if query_start_loc.dtype != torch.int32 or query_start_loc.dim() != 1:
+            raise TypeError("query_start_loc must be a 1-D int32 tensor")
+        if query_start_loc.numel() < n + 1:
+            raise ValueError("query_start_loc needs at least n + 1 entries")
+        query_start_loc = query_start_loc.contiguous()
+        tensors = tensors + (query_start_loc,)
+    for t in tensors:
         if not t.is_cuda:
             raise ValueError("paged_decode needs CUDA tensors (there is no CPU fallback)")
     if query.dtype != torch.bfloat16 or key_cache.dtype != torch.bfloat16 or value_cache.dtype != torch.bfloat16:
@@ -59,12 +71,13 @@ def paged_decode(query, key_cache, value_cache, block_table, seq_lens, scale, ou
     if workspace is None or workspace.numel() < nbytes:
         workspace = torch.empty(nbytes, dtype=torch.uint8, device=query.device)
     with torch.cuda.device(query.device):
-        check("ex_paged_decode", lib().ex_paged_decode(
+        check("ex_paged_decode", lib().ex_paged_decode_leading(
             query.data_ptr(), query.stride(0), query.stride(1), key_cache.data_ptr(), value_cache.data_ptr(),
             key_cache.stride(0), key_cache.stride(1), key_cache.stride(2), key_cache.shape[0], block_table.data_ptr(),
-            block_table.stride(0), seq_lens.data_ptr(), n, H, KV, D, BS, float(scale), MAX_LEN, split,
-            out.data_ptr(), out.stride(0), out.stride(1), _DT[out.dtype], workspace.data_ptr(), nbytes,
-            torch.cuda.current_stream(query.device).cuda_stream))
+            block_table.stride(0), seq_lens.data_ptr(),
+            None if query_start_loc is None else query_start_loc.data_ptr(), n, H, KV, D, BS, float(scale),
+            MAX_LEN, split, out.data_ptr(), out.stride(0), out.stride(1), _DT[out.dtype], workspace.data_ptr(),
+            nbytes, torch.cuda.current_stream(query.device).cuda_stream))
     return out
 
 
@@ -81,12 +94,21 @@ def kv_views(kv_cache: torch.Tensor, head_size: int):
     raise ValueError(f"unrecognised KV cache layout {tuple(kv_cache.shape)}")
 
 
+def mixed_step_requests(query_start_loc, block_table, seq_lens, out) -> int:
+    """Number of requests handed to the kernel in a mixed step: every request query_start_loc describes, bounded by
+    the rows of the block table, seq_lens and the output (shapes only: no device value is read). The kernel then
+    computes the leading one-token requests among them."""
+    return max(0, min(query_start_loc.shape[0] - 1, block_table.shape[0], seq_lens.shape[0], out.shape[0]))
+
+
 def install():
     """Patch vLLM's FlashAttentionImpl.forward (call before creating the LLM, with VLLM_ENABLE_V1_MULTIPROCESSING=0).
 
     Pure decode steps (max_query_len == 1) go entirely through paged_decode (CUDA-graph safe, no host sync). Mixed
     steps run vLLM's implementation first, then overwrite the leading decode tokens (vLLM orders decodes first) with
-    paged_decode, so every decode token is always computed by this kernel (reference paged_attn.py:141-160)."""
+    paged_decode, so every decode token is always computed by this kernel (reference paged_attn.py:141-160). The
+    reference counts those leading decodes on the host (an .item() sync); here the kernel reads query_start_loc and
+    finds them itself, so mixed steps are also free of host syncs."""
     from vllm.v1.attention.backends import flash_attn as fa
     orig = fa.FlashAttentionImpl.forward
     DEC = fa.AttentionType.DECODER
@@ -107,11 +129,10 @@ def install():
             return output
         res = orig(self, layer, query, key, value, kv_cache, attn_metadata, output, output_scale, output_block_scale)
         qsl = attn_metadata.query_start_loc
-        ql = qsl[1:] - qsl[:-1]
-        nd = int(torch.cumprod((ql == 1).to(torch.int32), 0).sum().item())
-        if nd > 0:
+        nreq = mixed_step_requests(qsl, attn_metadata.block_table, attn_metadata.seq_lens, out3)
+        if nreq > 0:
             paged_decode(query, key_cache, value_cache, attn_metadata.block_table, attn_metadata.seq_lens,
-                         self.scale, out3, nd, attn_metadata.max_seq_len)
+                         self.scale, out3, nreq, attn_metadata.max_seq_len, query_start_loc=qsl)
         return res
 
     fa.FlashAttentionImpl.forward = forward

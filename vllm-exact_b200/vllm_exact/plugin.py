@@ -12,6 +12,7 @@ slice, an int64 SUM all-reduce (exact under any reduction order) and the scaling
 all-reduce of that layer is switched off, because a sum of rounded partials is neither exact nor order-invariant.
 """
 import json
+import os
 from pathlib import Path
 
 import torch
@@ -29,6 +30,10 @@ TRUNC = True
 LMHEAD = True
 _TABLE = None
 RB = ops.RB  # rows per block: rows are independent, results unchanged, temporary memory bounded (plugin.py:24)
+# The reference keeps the bf16 weight beside its digits (plugin.py:72-79). VLLM_EXACT_DROP_BF16_WEIGHT=1 releases it
+# after digitization: weight memory goes from 4 to 2 bytes per element, at the price of no later weight reload. A
+# tied lm_head shares its tensor with the embedding, which keeps it (only this layer's reference is dropped).
+DROP_BF16_WEIGHT = os.environ.get("VLLM_EXACT_DROP_BF16_WEIGHT", "0") == "1"
 
 
 def load_table(path):
@@ -60,6 +65,16 @@ def _digitize_layer(layer):
     layer.register_buffer("ex_sw", sh.contiguous(), persistent=False)
     if _is_row_sharded(layer):
         layer.reduce_results = False  # the exact int64 all-reduce inside apply replaces vLLM's bf16 all-reduce
+    if DROP_BF16_WEIGHT:
+        drop_bf16_weight(layer)
+
+
+def drop_bf16_weight(layer):
+    """Replace layer.weight by an empty tensor of the same dtype and device (shape (0, K)); the digit buffers are the
+    only weights apply() reads. The parameter's attributes (weight_loader, ...) go with it."""
+    w = layer.weight
+    layer.weight = torch.nn.Parameter(torch.empty((0,) + tuple(w.shape[1:]), dtype=w.dtype, device=w.device),
+                                      requires_grad=False)
 
 
 def _apply(layer, x, bias):
