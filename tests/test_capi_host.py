@@ -69,3 +69,8 @@ def test_argument_validation_without_gpu(L):
     assert L.ex_paged_decode(*pd(64, 2, 128, None, 0)) == X.EX_ERR_UNSUPPORTED  # 32 query heads per KV head
     assert L.ex_paged_decode(*pd(32, 8, 128, None, 0)) == X.EX_ERR_WORKSPACE
     assert L.ex_paged_decode_workspace_bytes(2, 32, 128, 4096, 4096) >= 2 * 32 * (128 + 2) * 4
+    # mixed-step variant: query_start_loc inserted after seq_lens; int32 loads need a 4-byte aligned array
+    lead = lambda qsl: pd(32, 8, 128, None, 0)[:12] + (qsl,) + pd(32, 8, 128, None, 0)[12:]
+    assert L.ex_paged_decode_leading(*lead(ctypes.c_void_p(18))) == X.EX_ERR_ALIGN
+    assert L.ex_paged_decode_leading(*lead(ctypes.c_void_p(16))) == X.EX_ERR_WORKSPACE
+    assert L.ex_paged_decode_leading(*lead(None)) == X.EX_ERR_WORKSPACE  # NULL: plain decode of all n requests
