@@ -40,6 +40,8 @@ DECODE_M = [1, 16, 64]
 TENSOR_M = [256, 4096]
 ATTN = [(256, 1024), (64, 8192), (16, 16384)]
 METRIC = "exact-GEMM TB/s (exact_int8 linear, decode shapes M<=64 of the configs[1] sweep)"
+WORKLOAD = ("configs[1] decode sweep: M in {1,16,64} x (K,N) in {(4096,6144),(4096,4096),(4096,24576),"
+            "(12288,4096),(4096,151936)}, F=14 truncated, bf16 out")
 # DRAM bytes (read + write) per k_exact_tc_i8 launch, averaged over the 15 launches of one decode step, from the ncu
 # capture summarised in profiles/k_exact_tc_i8__decode_sweep.md (1.009 x the algorithmic bytes).
 GEMM_TRAFFIC_PER_LAUNCH = 331_717_905
@@ -244,8 +246,7 @@ def run_ours(args):
         "metric": METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8 digits (exact int32/int64), bf16 in/out", "data": "synthetic",
-        "config": {"workload": "configs[1] decode sweep: M in {1,16,64} x (K,N) in {(4096,6144),(4096,4096),"
-                               "(4096,24576),(12288,4096),(4096,151936)}, F=14 truncated, bf16 out",
+        "config": {"workload": WORKLOAD,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2: 1.63 GB of weight digits rotated between re-uses of a matrix",
                    "per_step_bytes": step_bytes, "timing": "CUDA graph of one step (15 x digitize + GEMM), "
@@ -571,7 +572,7 @@ def cpu_baseline(W=None, budget_s=20.0):
     return {"value": round(tot_bytes / tot_s / 1e12, 6), "unit": "TB/s", "cores": threads, "kind": "port",
             "sample": f"{runs} pass(es) of the 15 decode GEMMs with N capped at {ncap} output columns "
                       f"(digitize + exact integer GEMM + bf16), numpy oracle, {threads} host threads",
-            "seconds": round(tot_s, 2)}
+            "seconds": round(tot_s, 2), "passes": runs}
 
 
 def run_reference(args):
@@ -582,11 +583,13 @@ def run_reference(args):
     import numpy as np  # noqa: F401
     per = [cpu_baseline(budget_s=max(5.0, 60.0 / max(1, args.steps + args.warmup))) for _ in range(1)]
     v = per[0]["value"]
+    step_bytes = sum(gemm_bytes(M, K, N) for M in DECODE_M for name, K, N in SHAPES)
     print(json.dumps({
         "metric": METRIC, "value": v, "unit": "TB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": None, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "int64 (CPU)", "data": "synthetic", "impl": "reference",
-        "config": {"workload": "configs[1] decode sweep, bounded CPU sample", "parallelism": "cpu"},
+        "ms_per_step": round(step_bytes / (v * 1e12) * 1e3, 1), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int64 (CPU)", "data": "synthetic", "impl": "reference",
+        "config": {"workload": WORKLOAD, "parallelism": "cpu", "sample": per[0]["sample"], "per_step_bytes": step_bytes,
+                   "ms_per_step": "one full step's algorithmic bytes at the sampled rate"},
         "cpu_baseline": per[0], "e2e": {"value": v, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
