@@ -27,7 +27,8 @@ def nvcc() -> str:
 
 
 def sources():
-    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [ROOT / "include" / "vllm_exact_b200.h"]
+    return (sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) +
+            [ROOT / "include" / "vllm_exact_b200.h"])
 
 
 def up_to_date() -> bool:

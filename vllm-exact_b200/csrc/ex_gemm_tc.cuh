@@ -28,107 +28,9 @@
 // order.
 #pragma once
 #include "ex_common.cuh"
+#include "ex_tc_plan.h"
 
 namespace ex {
-
-constexpr int64_t EX_MAX_K = 65536;  // int32 accumulators: |md| <= 2^15 K must stay below 2^31
-constexpr int TC_EPI_WARPS = 8;  // two epilogue warps per TMEM lane quarter, splitting the token chunks
-constexpr int TC_THREADS = 64 + 32 * TC_EPI_WARPS;
-constexpr int TC_BK = 128;               // K bytes (int8 elements) per pipeline stage = one 128-byte swizzle row
-constexpr int TC_WTILE = 128 * TC_BK;    // bytes of one weight digit tile
-constexpr int TC_SMEM_BUDGET = 220 * 1024;
-constexpr int TC_TMEM_COLS = 512;
-constexpr int TC_RED_TOK = 4;  // tokens per bulk reduce-add (1 KB per warp)
-constexpr int TC_RED_STAGING = TC_EPI_WARPS * 2 * TC_RED_TOK * 32 * 8;  // per warp 2 buffers x 4 tokens x 32 rows x int64
-constexpr int TC_TOK_WORDS = TC_EPI_WARPS * 2 * 128 * 4;                // per warp (sx, cx) x up to 128 tokens x int32
-
-struct TcPlan {
-  int BT;        // token tile
-  int m_tiles, n_tiles, KI;
-  int64_t T;     // k-iterations of one m-tile row of tiles = n_tiles * KI
-  int gs;        // CTAs per group (one per m-tile of a chunk)
-  int groups;    // groups; group g walks (n-tile, k) range [T*g/groups, T*(g+1)/groups)
-  int chunks;    // passes over the range: m-tiles c*gs + j for c < chunks
-  int G;         // CTAs = groups * gs (* 2 for CTA pairs)
-  int pair;      // 1: CTA pairs (tcgen05 cta_group::2), n-tiles of 256 weight rows; BT = 128
-  int stages;
-  size_t smem;
-  size_t ws_bytes;
-  size_t cnt_bytes;
-};
-
-struct TcArgs {
-  const int32_t* cx;
-  const int32_t* sx;
-  const int32_t* cw;
-  const int32_t* sw;
-  void* out;
-  int64_t ldo;
-  long long* ws_acc;
-  int* ws_cnt;
-  int M, N, K;
-  int F, trunc, out_dtype, partial;
-  int m_tiles, n_tiles, KI;
-  int64_t T;  // n_tiles * KI
-  int gs, groups, chunks;
-  int stages;
-  int pair;  // 0 or 1: CTAs blockIdx.x and blockIdx.x ^ 1 form a pair that shares every tile
-};
-
-struct TcSeg {
-  int m_tile, n_tile, kb, ke;
-};
-
-// Segment walker shared by all roles. CTAs form groups of gs siblings; sibling j of group g walks the (n-tile,
-// k-iteration) range [T*g/groups, T*(g+1)/groups) once for each m-tile chunk c, on m-tile c*gs + j. Siblings run in
-// lockstep over the same weight k-slices, so a weight tile leaves HBM once per chunk and the other siblings read it
-// from L2 (one m-tile: the original one-range-per-CTA partition). 32-bit arithmetic whenever the products fit.
-struct TcWalk {
-  int64_t r0, r1, it;
-  int KI, j, mc, chunks, gs, m_tiles;
-  __device__ TcWalk(const TcArgs& a) {
-    const int u = (int)(blockIdx.x >> a.pair);  // both CTAs of a pair walk the same segments
-    const int g = u / a.gs;
-    j = u % a.gs;
-    if (a.T * (int64_t)a.groups < 2147483647ll) {
-      const uint32_t T = (uint32_t)a.T, G = (uint32_t)a.groups, b = (uint32_t)g;
-      r0 = (int64_t)((T * b) / G);
-      r1 = (int64_t)((T * (b + 1)) / G);
-    } else {
-      r0 = (a.T * (int64_t)g) / a.groups;
-      r1 = (a.T * (int64_t)(g + 1)) / a.groups;
-    }
-    it = r0;
-    KI = a.KI;
-    mc = 0;
-    chunks = a.chunks;
-    gs = a.gs;
-    m_tiles = a.m_tiles;
-  }
-  __device__ bool next(TcSeg& s) {
-    while (mc < chunks) {
-      const int m_tile = mc * gs + j;
-      if (m_tile >= m_tiles || it >= r1) {
-        ++mc;
-        it = r0;
-        continue;
-      }
-      if (it < 2147483647ll) {
-        const uint32_t u = (uint32_t)it, k = (uint32_t)KI;
-        s.n_tile = (int)(u / k);
-        s.kb = (int)(u % k);
-      } else {
-        s.n_tile = (int)(it / KI);
-        s.kb = (int)(it % KI);
-      }
-      s.m_tile = m_tile;
-      s.ke = (int)min((int64_t)KI, (int64_t)s.kb + (r1 - it));
-      it += s.ke - s.kb;
-      return true;
-    }
-    return false;
-  }
-};
 
 // sxs / cxs: this tile's per-token scale words, already in shared memory; swn / cwn: this weight row's.
 // All CW values are converted first with straight-line float64 code (ex_scale_to_f32: exact int64 -> float64, exact
@@ -273,7 +175,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // this is safe even if the previous kernel wrote them); every shared-memory load, every read of activations or
   // scales and every write happens after pdl_wait().
   if (warp == 0 && lane == 0) {
-    TcWalk walk(a);
+    TcWalk walk(a, (int)blockIdx.x);
     TcSeg sg;
     int left = S;
     while (left > 0 && walk.next(sg)) {
@@ -292,7 +194,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (lane == 0) {
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
-      TcWalk walk(a);
+      TcWalk walk(a, (int)blockIdx.x);
       TcSeg sg;
       int stage = 0;
       uint32_t phase = 0;
@@ -351,7 +253,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t idesc_2bt = make_idesc_i8(128, 2 * BT);
       const uint32_t idesc_bt = make_idesc_i8(128, BT);
       const uint32_t idesc_pair = make_idesc_i8(256, BT);
-      TcWalk walk(a);
+      TcWalk walk(a, (int)blockIdx.x);
       TcSeg sg;
       int stage = 0;
       uint32_t phase = 0;
@@ -431,7 +333,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     constexpr int CW = BT < 32 ? 8 : 16;  // TMEM columns per tcgen05.ld (and tokens per chunk)
     constexpr int NCH = BT / CW;          // chunks per tile; this warp takes chunks half, half + 2, ...
     uint32_t nbulk = 0;  // bulk reduce-adds issued by this warp (selects and recycles the staging buffers)
-    TcWalk walk(a);
+    TcWalk walk(a, (int)blockIdx.x);
     TcSeg sg;
     int seg_i = 0;
     uint32_t epi_phase = 0;
@@ -457,12 +359,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       // Slot layout: [lane quarter][token][32 rows].
       // A split tile (m, n) owns slot (b* - 1) * m_tiles + m, b* = the first group boundary strictly inside n's
       // k-range: every contributor computes the same slot and distinct split tiles get distinct slots.
-      int slot = 0;
-      if (!whole) {
-        const int64_t num = ((int64_t)n_tile * a.KI + 1) * a.groups + a.T - 1;
-        const int bstar = num < 2147483647ll ? (int)((uint32_t)num / (uint32_t)a.T) : (int)(num / a.T);
-        slot = (bstar - 1) * a.m_tiles + m_tile;
-      }
+      int slot = whole ? 0 : tc_split_slot(a, n_tile, m_tile);
       if (PAIR) slot = 2 * slot + (int)rank;  // each CTA of a pair owns the half of the slot holding its rows
       long long* slot_q = a.ws_acc + ((int64_t)slot * 4 + q) * BT * 32;
       // the pair's TMEM-empty barrier lives in the even CTA (the MMA issuer)
@@ -623,61 +520,6 @@ static bool tc_supported(const int8_t* xh, const int8_t* xl, int64_t ldx, const 
   return device_is_sm100();
 }
 
-static int tc_pick_bt(int64_t M) {
-  if (M <= 8) return 8;
-  if (M <= 16) return 16;
-  if (M <= 32) return 32;
-  if (M <= 64) return 64;
-  return 128;
-}
-
-static size_t tc_stage_bytes(int BT, bool pair) {
-  return 2 * (size_t)TC_WTILE + 2 * (size_t)(pair ? BT / 2 : BT) * TC_BK;
-}
-
-// EX_ALGO_TC_I8_PAIR plans CTA pairs on 256-row n-tiles and 128-token m-tiles; every other algorithm value plans
-// single CTAs with the token tile picked from M.
-static TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int split_k, int algo, int sms) {
-  TcPlan p;
-  const bool pair = (algo == EX_ALGO_TC_I8_PAIR);
-  p.pair = pair ? 1 : 0;
-  p.BT = pair ? 128 : tc_pick_bt(M);
-  p.m_tiles = (int)((M + p.BT - 1) / p.BT);
-  p.n_tiles = pair ? (int)((N + 255) / 256) : (int)((N + 127) / 128);
-  p.KI = (int)((K + TC_BK - 1) / TC_BK);
-  p.T = (int64_t)p.n_tiles * p.KI;
-  p.gs = std::min(p.m_tiles, 8);
-  p.chunks = (p.m_tiles + p.gs - 1) / p.gs;
-  const int units = pair ? sms / 2 : sms;  // CTA pairs or CTAs resident at once (one per SM)
-  const int64_t fit = std::max<int64_t>(1, units / p.gs);  // groups resident at once
-  int64_t groups = fit;  // automatic default: the balanced (n-tile, k-step) partition over every resident group
-  if (split_k > 0) {
-    groups = (int64_t)p.n_tiles * split_k;
-  } else {
-    // Tile-aligned partition when it keeps at least 60% of the groups busy: every n-tile split into s equal K ranges
-    // (s = 1: whole tiles, no workspace). Fewer, aligned split tiles cost less in reduction and finishing than the
-    // balanced partition's ragged ones; measured on B200 it wins for the narrow layers (o_proj M=64 17.5 -> 15.2 us,
-    // qkv M=256 34.6 -> 26.6 us) and is not taken for wide ones (gate_up, lm_head), where it would not apply.
-    const int64_t s = fit / p.n_tiles;
-    if (s >= 1 && (int64_t)p.n_tiles * s * 10 >= fit * 6) groups = (int64_t)p.n_tiles * s;
-  }
-  groups = std::max<int64_t>(1, std::min<int64_t>(groups, p.T));
-  groups = std::min<int64_t>(groups, 2147483647 / p.gs);
-  p.groups = (int)groups;
-  p.G = p.groups * p.gs * (pair ? 2 : 1);
-  const size_t stage = tc_stage_bytes(p.BT, pair);
-  const size_t overhead = 1024 + 256 + TC_RED_STAGING + TC_TOK_WORDS;  // alignment, barriers, staging, scale words
-  p.stages = (int)std::min<size_t>(8, (TC_SMEM_BUDGET - overhead) / stage);
-  p.smem = (size_t)p.stages * stage + overhead;
-  const bool aligned = (groups <= p.n_tiles) && (p.n_tiles % groups == 0);  // every group covers whole n-tiles
-  const int64_t slots = (groups - 1) * (int64_t)p.m_tiles;  // one per (group boundary, m-tile)
-  const int halves = pair ? 2 : 1;                           // a pair's slot has one half per CTA (128 rows each)
-  p.cnt_bytes = (size_t)((slots * halves * 4 + 255) / 256 * 256);
-  p.ws_bytes = (aligned || slots == 0) ? 0 : p.cnt_bytes + (size_t)slots * halves * p.BT * 128 * 8;
-  // (slot layout [4 lane quarters][BT tokens][32 rows] per 128 rows: each epilogue warp reduces contiguous 1 KB)
-  return p;
-}
-
 static bool encode_2d_i8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld_bytes,
                          uint32_t box_inner, uint32_t box_outer) {
   PFN_encodeTiled enc = get_encode_fn();
@@ -728,15 +570,7 @@ static cudaError_t launch_tc(const TcPlan& p, int F, int trunc, int out_dtype, c
   a.trunc = trunc ? 1 : 0;
   a.out_dtype = out_dtype;
   a.partial = PARTIAL ? 1 : 0;
-  a.m_tiles = p.m_tiles;
-  a.n_tiles = p.n_tiles;
-  a.KI = p.KI;
-  a.T = p.T;
-  a.gs = p.gs;
-  a.groups = p.groups;
-  a.chunks = p.chunks;
-  a.stages = p.stages;
-  a.pair = p.pair;
+  tc_plan_args(p, a);
   if (p.pair) return launch_tc_bt<128, true>(p, a, mwh, mwl, mxh, mxl, st);
   switch (p.BT) {
     case 8: return launch_tc_bt<8>(p, a, mwh, mwl, mxh, mxl, st);
