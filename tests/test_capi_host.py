@@ -74,3 +74,20 @@ def test_argument_validation_without_gpu(L):
     assert L.ex_paged_decode_leading(*lead(ctypes.c_void_p(18))) == X.EX_ERR_ALIGN
     assert L.ex_paged_decode_leading(*lead(ctypes.c_void_p(16))) == X.EX_ERR_WORKSPACE
     assert L.ex_paged_decode_leading(*lead(None)) == X.EX_ERR_WORKSPACE  # NULL: plain decode of all n requests
+    # fused tensor-parallel epilogue: rank outside [0, world), world < 1, bad dtype, leading dimensions < N, NULL
+    ar = lambda rank, world, od, ldt, ldo, M=4, N=8, parts=p: (parts, ldt, p, p, rank, world, p, p, M, N, p, od, ldo,
+                                                              None)
+    assert L.ex_allreduce_epilogue_i64(*ar(2, 2, 1, 8, 8)) == X.EX_ERR_ARG
+    assert L.ex_allreduce_epilogue_i64(*ar(0, 0, 1, 8, 8)) == X.EX_ERR_ARG
+    assert L.ex_allreduce_epilogue_i64(*ar(-1, 2, 1, 8, 8)) == X.EX_ERR_ARG
+    assert L.ex_allreduce_epilogue_i64(*ar(0, 2, 9, 8, 8)) == X.EX_ERR_DTYPE
+    assert L.ex_allreduce_epilogue_i64(*ar(0, 2, 1, 4, 8)) == X.EX_ERR_ARG
+    assert L.ex_allreduce_epilogue_i64(*ar(0, 2, 1, 8, 4)) == X.EX_ERR_ARG
+    assert L.ex_allreduce_epilogue_i64(*ar(0, 2, 1, 8, 8, M=-1)) == X.EX_ERR_ARG
+    assert L.ex_allreduce_epilogue_i64(*ar(0, 2, 1, 8, 8, parts=None)) == X.EX_ERR_ARG
+    # IPC helpers: NULL arguments are rejected before any driver call
+    off = ctypes.c_uint64(0)
+    assert L.ex_ipc_get_handle(None, ctypes.create_string_buffer(X.EX_IPC_HANDLE_BYTES), ctypes.byref(off)) == X.EX_ERR_ARG
+    assert L.ex_ipc_get_handle(p, None, ctypes.byref(off)) == X.EX_ERR_ARG
+    assert L.ex_ipc_open_handle(None, ctypes.byref(ctypes.c_void_p())) == X.EX_ERR_ARG
+    assert L.ex_ipc_close_handle(None) == X.EX_ERR_ARG
