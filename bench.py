@@ -270,9 +270,11 @@ def run_ours(args):
         e2e["h2d_bytes_per_step"] *= world
         e2e["d2h_bytes_per_step"] *= world
     result["e2e"] = e2e
+    # every rank runs the per-kernel sections on its own GPU (rank 0 reports them), so all ranks reach the final
+    # barrier together instead of waiting inside an NCCL collective for rank 0 alone
+    result["sweep_tensor"] = tensor_sweep(dev, W, bf16_burst, args.quick)
+    result["attention"] = attention_bench(dev, hbm, args.quick)
     if rank == 0:
-        result["sweep_tensor"] = tensor_sweep(dev, W, bf16_burst, args.quick)
-        result["attention"] = attention_bench(dev, hbm, args.quick)
         if world == 1 and not args.quick:
             del W, X, Y
             torch.cuda.empty_cache()
