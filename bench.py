@@ -801,6 +801,8 @@ def run_case(args):
                                     out=y)
     elif kind == "step":
         print(json.dumps(decode_step_bench(dev)), flush=True)
+    elif kind == "attnbench":  # the attention section of the default run alone (BASELINE config 4 batches)
+        print(json.dumps(attention_bench(dev, peaks()[0], False)), flush=True)
     elif kind == "attn":
         n, ctx = int(rest[0]), int(rest[1])
         PA.MAX_LEN = 20480

@@ -203,19 +203,20 @@ bool encode_kv_map(CUtensorMap* map, const void* base, int D, int KV, int BS, in
 }
 
 int launch_merge(const float* ws_m, const float* ws_l, const float* ws_acc, void* out, int64_t so_t, int64_t so_h,
-                 int n, int H, int NS, int D, int out_dtype, const int32_t* qsl, cudaStream_t st) {
+                 int n, int H, int NS, int D, int out_dtype, const int32_t* seq_lens, int split, const int32_t* qsl,
+                 cudaStream_t st) {
   const int mthreads = std::min(D, 256);
   const dim3 mg(n * H), mb(mthreads);
   cudaError_t e;
   if (out_dtype == EX_DTYPE_BF16)
     e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_BF16>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D,
-                      qsl);
+                      seq_lens, split, qsl);
   else if (out_dtype == EX_DTYPE_F16)
     e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_F16>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D,
-                      qsl);
+                      seq_lens, split, qsl);
   else
     e = ex_launch_pdl(ex::k_paged_merge<EX_DTYPE_F32>, mg, mb, 0, st, ws_m, ws_l, ws_acc, out, so_t, so_h, H, NS, D,
-                      qsl);
+                      seq_lens, split, qsl);
   if (e != cudaSuccess) return cuda_status(e);
   return cuda_status(cudaGetLastError());
 }
@@ -502,7 +503,8 @@ int ex_paged_decode_leading(const void* q, int64_t sq_t, int64_t sq_h, const voi
       else EX_PT_LAUNCH(128)
 #undef EX_PT_LAUNCH
       if (e != cudaSuccess) return cuda_status(e);
-      return launch_merge(ws_m, ws_l, ws_acc, out, so_t, so_h, n, H, NS, D, out_dtype, query_start_loc, st);
+      return launch_merge(ws_m, ws_l, ws_acc, out, so_t, so_h, n, H, NS, D, out_dtype, seq_lens, split,
+                        query_start_loc, st);
     }
   }
 #define EX_PD_LAUNCH(DD)                                                                                         \
@@ -520,7 +522,8 @@ int ex_paged_decode_leading(const void* q, int64_t sq_t, int64_t sq_h, const voi
 #undef EX_PD_LAUNCH
   if (e != cudaSuccess) return cuda_status(e);
   if ((e = cudaGetLastError()) != cudaSuccess) return cuda_status(e);
-  return launch_merge(ws_m, ws_l, ws_acc, out, so_t, so_h, n, H, NS, D, out_dtype, query_start_loc, st);
+  return launch_merge(ws_m, ws_l, ws_acc, out, so_t, so_h, n, H, NS, D, out_dtype, seq_lens, split,
+                        query_start_loc, st);
 }
 
 }  // extern "C"

@@ -9,8 +9,10 @@
 //   p = exp(S*scale - m), p_hi = bf16(p), p_lo = bf16(p - p_hi)
 //   O = O*alpha + p_hi.V + p_lo.V    two bf16 tensor-core products, i.e. p is used to ~16 bits
 // The warps are merged in fixed order and the segment's (m, l, acc) is written to the partial workspace.
-// Kernel 2 (k_paged_merge), one CTA per (request, head): merges the NS = ceil(max_len / split) segments in fixed
-// order s = 0..NS-1 and writes acc / l.
+// Kernel 2 (k_paged_merge), one CTA per (request, head): merges the request's non-empty segments in fixed order
+// s = 0 .. min(NS, ceil(L / split)) - 1 (NS = ceil(max_len / split) segment CTAs per request are launched; those past
+// the request's length exit at once without writing) and writes acc / l. Merging an empty segment would be an exact
+// no-op at the end of the fixed order, so stopping before the empty ones changes no bits.
 // Nothing in either kernel depends on n, on other requests, or on where pages live, so a request's output is
 // bitwise the same alone, in any batch, and under any page placement.
 #pragma once
@@ -103,14 +105,7 @@ __global__ void __launch_bounds__(PD_THREADS, 2)
   const int end = min(start + split, L);
   const int64_t pbase = ((int64_t)b * H + (int64_t)g * G) * NS + s;  // partial index of row 0
 
-  if (start >= end) {  // empty segment: contributes exactly nothing to the merge
-    for (int i = tid; i < G * D; i += PD_THREADS) ws_acc[(pbase + (int64_t)(i / D) * NS) * D + (i % D)] = 0.0f;
-    for (int r = tid; r < G; r += PD_THREADS) {
-      ws_m[pbase + (int64_t)r * NS] = -INFINITY;
-      ws_l[pbase + (int64_t)r * NS] = 0.0f;
-    }
-    return;
-  }
+  if (start >= end) return;  // empty segment (s >= ceil(L / split)): the merge stops before it, nothing to write
 
   const uint32_t smem0 = ex_smem_u32(pd_smem);
   const __nv_bfloat16* kbase = kc + (int64_t)g * s_head;
@@ -321,15 +316,18 @@ __global__ void __launch_bounds__(PD_THREADS, 2)
 template <int OUT_DTYPE>
 __global__ void k_paged_merge(const float* __restrict__ ws_m, const float* __restrict__ ws_l,
                               const float* __restrict__ ws_acc, void* out, int64_t so_t, int64_t so_h, int H, int NS,
-                              int D, const int32_t* __restrict__ qsl) {
+                              int D, const int32_t* __restrict__ seq_lens, int split,
+                              const int32_t* __restrict__ qsl) {
   pdl_launch_dependents();
   pdl_wait();
   const int bh = blockIdx.x;
   const int b = bh / H, h = bh % H;
   if (qsl != nullptr && !pd_in_leading_decodes(qsl, b)) return;  // row b belongs to a prefill: left untouched
+  const int L = seq_lens[b];
+  const int ns = L > 0 ? min(NS, (int)(((int64_t)L + split - 1) / split)) : 0;  // non-empty segments (L = 0: none)
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float m = -INFINITY, l = 0.0f, acc = 0.0f;
-    for (int s = 0; s < NS; ++s) {
+    for (int s = 0; s < ns; ++s) {
       const int64_t pi = (int64_t)bh * NS + s;
       const float ms = ws_m[pi];
       const float ls = ws_l[pi];

@@ -76,14 +76,7 @@ __global__ void __launch_bounds__(PT_THREADS, 2)
   const int end = min(start + split, L);
   const int64_t pbase = ((int64_t)b * H + (int64_t)g * G) * NS + s;  // partial index of query head g*G
 
-  if (start >= end) {  // empty segment: contributes exactly nothing to the merge
-    for (int i = tid; i < G * D; i += PT_THREADS) ws_acc[(pbase + (int64_t)(i / D) * NS) * D + (i % D)] = 0.0f;
-    for (int r = tid; r < G; r += PT_THREADS) {
-      ws_m[pbase + (int64_t)r * NS] = -INFINITY;
-      ws_l[pbase + (int64_t)r * NS] = 0.0f;
-    }
-    return;
-  }
+  if (start >= end) return;  // empty segment (s >= ceil(L / split)): the merge stops before it, nothing to write
   const int nblk = (end - start + PT_BLK - 1) / PT_BLK;
   if (tid == 0) {
     for (int i = 0; i < C::STAGES; ++i) {
