@@ -11,8 +11,9 @@
 // The warps are merged in fixed order and the segment's (m, l, acc) is written to the partial workspace.
 // Kernel 2 (k_paged_merge), one CTA per (request, head): merges the request's non-empty segments in fixed order
 // s = 0 .. min(NS, ceil(L / split)) - 1 (NS = ceil(max_len / split) segment CTAs per request are launched; those past
-// the request's length exit at once without writing) and writes acc / l. Merging an empty segment would be an exact
-// no-op at the end of the fixed order, so stopping before the empty ones changes no bits.
+// the request's length exit at once without writing) and writes acc / l. Merging an empty segment at the end of the
+// fixed order only adds +0 to acc and l, so stopping before the empty ones changes no bits (an exactly -0.0 output
+// keeps its sign). The stopping point depends on the request's own length only, so invariance is unaffected.
 // Nothing in either kernel depends on n, on other requests, or on where pages live, so a request's output is
 // bitwise the same alone, in any batch, and under any page placement.
 #pragma once
