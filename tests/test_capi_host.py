@@ -91,3 +91,14 @@ def test_argument_validation_without_gpu(L):
     assert L.ex_ipc_get_handle(p, None, ctypes.byref(off)) == X.EX_ERR_ARG
     assert L.ex_ipc_open_handle(None, ctypes.byref(ctypes.c_void_p())) == X.EX_ERR_ARG
     assert L.ex_ipc_close_handle(None) == X.EX_ERR_ARG
+
+
+def test_exact_cfgs_parse():
+    """Every autotuning candidate is a configuration exact_linear accepts (algorithm, split-K), and reference-style
+    tuples keep their meaning (split-K at index 6, MMA kind at index 7)."""
+    from vllm_exact import kernels as K
+    seen = {K._parse_cfg(c) for c in K.EXACT_CFGS}
+    assert len(seen) == len(K.EXACT_CFGS)
+    assert all(a in (K.EX_ALGO_TC_I8, K.EX_ALGO_TC_I8_PAIR, K.EX_ALGO_SIMT) and sk >= 0 for a, sk in seen)
+    assert K._parse_cfg(None) == (K.EX_ALGO_AUTO, 0)
+    assert K._parse_cfg((64, 128, 128, 4, 4, 8, 4, 0)) == (K.EX_ALGO_TC_I8, 4)

@@ -131,6 +131,28 @@ def test_unaligned_leading_dimension_uses_simt(K):
     with pytest.raises(_lib.ExactError) as ei:
         _run(K, xd, wd, 14, True, "tc_i8", 0)
     assert ei.value.status == _lib.EX_ERR_ALIGN
+    key = (M, N, Kd, 14, True)  # the autotuner skips the configurations these digits cannot run
+    try:
+        assert K.autotune_exact(xd, wd, 14, True)["algo"] == K.EX_ALGO_SIMT
+    finally:
+        K._CFG_CACHE.pop(key, None)
+
+
+def test_autotune_exact_keeps_bits(K, golden):
+    """autotune_exact (reference kernels.py:292-316) times EXACT_CFGS, remembers the fastest for the shape, and
+    exact_linear(cfg=None) then uses it: config 1's bf16 output still hashes to the reference's golden sha256."""
+    x, w = R.config1()
+    xd, wd = K.digitize(x.to(DEV), 14), K.digitize(w.to(DEV), 14)
+    key = (8, 1024, 1024, 14, True)
+    K._CFG_CACHE.pop(key, None)
+    try:
+        cfg = K.autotune_exact(xd, wd, 14, True)
+        assert cfg in K.EXACT_CFGS and K._CFG_CACHE[key] == cfg
+        y = torch.empty(8, 1024, device=DEV, dtype=torch.bfloat16)
+        K.exact_linear(xd, wd, 14, True, out=y)
+        assert R.sha(y) == golden["config1"]["y_bf16_sha"]
+    finally:
+        K._CFG_CACHE.pop(key, None)
 
 
 def test_batch_invariance_rows(K):

@@ -26,8 +26,8 @@ from . import _lib
 from ._lib import EX_ALGO_AUTO, EX_ALGO_SIMT, EX_ALGO_TC_BF16, EX_ALGO_TC_I8, EX_ALGO_TC_I8_PAIR, check, lib
 
 __all__ = ["digitize", "digitize_weight", "exact_linear", "exact_linear_partial_i64", "exact_epilogue",
-           "reserve_workspace", "EX_ALGO_AUTO", "EX_ALGO_SIMT", "EX_ALGO_TC_I8", "EX_ALGO_TC_BF16",
-           "EX_ALGO_TC_I8_PAIR"]
+           "autotune_exact", "EXACT_CFGS", "reserve_workspace", "EX_ALGO_AUTO", "EX_ALGO_SIMT", "EX_ALGO_TC_I8",
+           "EX_ALGO_TC_BF16", "EX_ALGO_TC_I8_PAIR"]
 
 _DT = {torch.float32: _lib.EX_DTYPE_F32, torch.bfloat16: _lib.EX_DTYPE_BF16, torch.float16: _lib.EX_DTYPE_F16}
 _LD_ALIGN = 16  # digit rows are padded to 16 bytes so the tensor-core kernels can TMA them
@@ -151,10 +151,51 @@ def _operands(xd, wd):
     return xh, xl, cx, sx, wh, wl, cw, sw
 
 
+# Candidate configurations of autotune_exact. The reference lists Triton tile configurations here
+# (kernels.py:250-253); the B200 kernels choose their tiles from the shape, so a configuration selects what is left
+# free: the algorithm and the split-K factor (0 = the automatic plan of that algorithm). Every one gives the same bits.
+EXACT_CFGS = ([{"algo": EX_ALGO_TC_I8, "split_k": s} for s in (0, 1, 2, 4, 8)] +
+              [{"algo": EX_ALGO_TC_I8_PAIR, "split_k": s} for s in (0, 1, 2)] +
+              [{"algo": EX_ALGO_SIMT, "split_k": 0}])
+_CFG_CACHE = {}  # (M, N, K, F, trunc) -> configuration chosen by autotune_exact
+
+
+def autotune_exact(xd, wd, F: int, trunc: bool):
+    """Time every configuration of EXACT_CFGS on these operands (one warm-up call, then 10 calls between CUDA events
+    on the current stream), remember the fastest for (M, N, K, F, trunc) and return it (reference kernels.py:292-316).
+    Configurations the operands do not support (e.g. tensor-core algorithms on unaligned digits) are skipped.
+    exact_linear(cfg=None) uses the remembered configuration; without a tuning call it takes the automatic plan, so
+    nothing is ever timed inside a CUDA-graph capture. The choice changes speed only, never result bits."""
+    xh, wh = xd[0], wd[0]
+    M, K = xh.shape
+    N = wh.shape[0]
+    best = None
+    for c in EXACT_CFGS:
+        try:
+            exact_linear(xd, wd, F, trunc, cfg=c)
+            torch.cuda.synchronize(xh.device)
+            st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            st.record()
+            for _ in range(10):
+                exact_linear(xd, wd, F, trunc, cfg=c)
+            en.record()
+            torch.cuda.synchronize(xh.device)
+            t = st.elapsed_time(en)
+        except _lib.ExactError:
+            continue
+        if best is None or t < best[0]:
+            best = (t, c)
+    if best is None:
+        raise RuntimeError("autotune_exact: no configuration runs on these operands")
+    _CFG_CACHE[(M, N, K, F, bool(trunc))] = best[1]
+    return best[1]
+
+
 def exact_linear(xd, wd, F: int, trunc: bool = False, out: torch.Tensor | None = None, cfg=None) -> torch.Tensor:
     """Exact linear layer y = x . w^T from digits (reference kernels.py:257-289). Returns fp32 (M, N) unless `out`
     (fp32, bf16 or fp16; row-major) is given. Bitwise identical to the reference's exact_linear_torch for every
-    cfg (algorithm / split-K)."""
+    cfg (algorithm / split-K). cfg=None: the configuration autotune_exact chose for this shape, else the automatic
+    plan."""
     xh, xl, cx, sx, wh, wl, cw, sw = _operands(xd, wd)
     M, K = xh.shape
     N = wh.shape[0]
@@ -162,6 +203,8 @@ def exact_linear(xd, wd, F: int, trunc: bool = False, out: torch.Tensor | None =
         out = torch.empty((M, N), device=xh.device, dtype=torch.float32)
     if out.dtype not in _DT or out.shape != (M, N) or (out.numel() and out.stride(1) != 1):
         raise ValueError("out must be a row-major (M, N) fp32/bf16/fp16 tensor")
+    if cfg is None and _CFG_CACHE:
+        cfg = _CFG_CACHE.get((M, N, K, F, bool(trunc)))
     algo, sk = _parse_cfg(cfg)
     L = lib()
     with torch.cuda.device(xh.device):
