@@ -177,3 +177,20 @@ def test_mixed_step_graph_replay_follows_query_start_loc(P):
         assert torch.equal(o[:nd], full[:nd]), ql
         assert bool((o[nd:] == 7.0).all()), ql
     del g
+
+
+@pytest.mark.parametrize("H,KV,D", [(32, 8, 128), (16, 4, 256)])  # TMA page-gather kernel, cp.async kernel
+def test_kv_head_sharding_bitwise(P, H, KV, D):
+    """Tensor parallelism shards attention by KV head with no communication: each half of the KV heads, with its query
+    heads, computed on its own (strided views of the same cache, as a rank sees its shard) gives bitwise the rows of
+    the full computation."""
+    B, BS = 8, 16
+    q, kv, bt, sl = _case(B, 900, BS, H, KV, D, jitter=True)
+    kc, vc = R.kv_views(kv, D)
+    full = torch.empty(B, H, D, device=DEV, dtype=torch.bfloat16)
+    P.paged_decode(q, kc, vc, bt, sl, 0.1, full, B)
+    for r in range(2):
+        k0, k1, h0, h1 = r * KV // 2, (r + 1) * KV // 2, r * H // 2, (r + 1) * H // 2
+        o = torch.empty(B, H // 2, D, device=DEV, dtype=torch.bfloat16)
+        P.paged_decode(q[:, h0:h1], kc[:, :, k0:k1], vc[:, :, k0:k1], bt, sl, 0.1, o, B)
+        assert torch.equal(o, full[:, h0:h1]), r
