@@ -2,7 +2,6 @@
 
 Tests marked `gpu` need a CUDA device and the built library; everything else runs on CPU.
 """
-import os
 import sys
 from pathlib import Path
 

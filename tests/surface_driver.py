@@ -48,7 +48,7 @@ def check_plugin():
 
     import recipes as R
     from oracle import exact_oracle as O
-    from vllm_exact import kernels as K, paged_attn as P, plugin
+    from vllm_exact import paged_attn as P, plugin
     dev = torch.device("cuda", 0)
     out = {}
     cfg = plugin.ExactInt8Config()

@@ -9,7 +9,6 @@ must have left zeroed), and that a shape needing more scratch than the static ar
 
 The file is named so that pytest collects it last.
 """
-import ctypes
 
 import pytest
 import torch

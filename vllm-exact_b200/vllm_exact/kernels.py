@@ -17,7 +17,6 @@ used to check this module lives in the repository's oracle/ directory (test infr
 """
 from __future__ import annotations
 
-import ctypes
 import threading
 
 import torch
