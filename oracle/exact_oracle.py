@@ -15,6 +15,10 @@ Parity pin: tests/test_oracle_golden.py checks this module against golden vector
 (tests/golden/make_golden.py imports the reference and records its outputs), including the sha256 of the
 configuration-1 bf16 output.
 
+A second restatement in plain C with integer-only dot products (exact_oracle_int.c, wrapped by c_oracle.py) is
+checked against the same golden vectors and against this module on full-range digits at K = 65536
+(tests/test_oracle_c.py).
+
 Integer dot products are computed with float64 BLAS matrix products. This is exact: every digit is an integer with
 |d| <= 128, so every product is an integer with |p| <= 2^14 and every partial sum of K terms is an integer with
 |s| <= K * 2^14, far below 2^53 for any K this code is used with (checked below). Integers below 2^53 are represented
