@@ -769,7 +769,8 @@ def tp_case(args):
 def run_case(args):
     """Workloads for ncu captures, run eagerly --reps times (ncu flushes caches before each captured pass):
     `gemm:<shape>:<M>[:<algo>]` one GEMM, `attn:<n>:<ctx>` one attention batch, `sweep` the 15 GEMMs of the headline
-    decode step."""
+    decode step. Timed sections alone: `step` the config-5 hot-path share, `attnbench` the config-4 attention
+    batches, `engine:exact|plain` config 5 through the vLLM engine, `tp` the row-parallel layer under torchrun."""
     if args.case.startswith("engine"):
         return engine_case(args)
     if args.case == "tp":
@@ -915,7 +916,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--quick", action="store_true", help="skip the slow secondary measurements")
-    ap.add_argument("--case", default=None, help="profiling workload, e.g. gemm:o_proj:64 or attn:64:8192")
+    ap.add_argument("--case", default=None, help="profiling workload or single section, e.g. gemm:o_proj:64, "
+                    "attn:64:8192, sweep, step, attnbench, engine:exact, tp")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--ref-triton", action="store_true",
                     help="time the reference's Triton kernels (installed under baseline/_ref) against ours")
