@@ -102,3 +102,21 @@ def test_exact_cfgs_parse():
     assert all(a in (K.EX_ALGO_TC_I8, K.EX_ALGO_TC_I8_PAIR, K.EX_ALGO_SIMT) and sk >= 0 for a, sk in seen)
     assert K._parse_cfg(None) == (K.EX_ALGO_AUTO, 0)
     assert K._parse_cfg((64, 128, 128, 4, 4, 8, 4, 0)) == (K.EX_ALGO_TC_I8, 4)
+
+
+def test_header_is_plain_c_and_links(tmp_path):
+    """tests/c_abi_check.c includes the header as strict C99 (-pedantic-errors), links the library and calls the entry
+    points that answer before touching a device: the boundary is a C ABI any FFI can bind, not a C++ one."""
+    import shutil
+    import subprocess
+    from vllm_exact import _lib
+    gcc = shutil.which("gcc")
+    if gcc is None or not _lib.LIB_PATH.exists():
+        pytest.skip("gcc or the built library is missing")
+    exe = tmp_path / "c_abi_check"
+    libdir = str(_lib.LIB_PATH.parent)
+    subprocess.run([gcc, "-std=c99", "-Wall", "-Wextra", "-Werror", "-pedantic-errors", "-I", str(ROOT / "include"),
+                    str(ROOT / "tests" / "c_abi_check.c"), "-L", libdir, "-l" + _lib.LIB_PATH.stem[3:],
+                    "-Wl,-rpath," + libdir, "-o", str(exe)], check=True, capture_output=True, text=True, timeout=120)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0 and r.stdout.strip() == "OK", (r.returncode, r.stdout, r.stderr)
