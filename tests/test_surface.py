@@ -57,3 +57,18 @@ def test_plugin_methods_and_attention_patch_on_gpu():
     assert r["patch_max_err"] < 1e-3
     assert r["mixed_nd"] == 3  # mixed step: leading decodes found on the device, the rest left to vLLM's forward
     assert r["mixed_decodes_match"] is True and r["mixed_rest_from_vllm"] is True
+
+
+def test_custom_op_fake_impl_for_tracing():
+    """exactmm::linear carries a fake implementation (reference plugin.py:67-69), so torch.compile / graph tracing sees
+    (*, K) -> (*, N) in x's dtype without running the kernel; checked under FakeTensorMode, no GPU or library needed."""
+    import torch
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    import vllm_exact.ops  # noqa: F401  (registers the op; importing it loads no library)
+    with FakeTensorMode():
+        for shape, dt in (((2, 5, 4096), torch.bfloat16), ((7, 4096), torch.float16), ((0, 4096), torch.bfloat16)):
+            x = torch.empty(*shape, dtype=dt)
+            w = [torch.empty(6144, 4096, dtype=torch.int8) for _ in range(2)]
+            s = [torch.empty(6144, dtype=torch.int32) for _ in range(2)]
+            y = torch.ops.exactmm.linear(x, w[0], w[1], s[0], s[1])
+            assert tuple(y.shape) == shape[:-1] + (6144,) and y.dtype == dt
