@@ -13,8 +13,13 @@ Also reported (not part of `value`): the tensor-bound sweep M in {256, 4096} as 
 flops (6 M N K) against the measured bf16 dense peak, the paged decode attention of configs[3], the end-to-end rate
 through the public op with host copies, the CPU oracle on a bounded sample, and the SM clocks during the run.
 
---impl reference times the reference's CPU integer path (restated in oracle/, numpy) on a bounded sample of the same
-workload with all host threads, and prints the same metric.
+After the timed region, rank 0 checks the step's outputs bit for bit against the CPU oracle on a row sample
+(`bitwise_ok`), times the reference's own Triton kernels on the same digits (`ref_triton`), and times the reference's
+CPU integer path on a bounded sample (`cpu_baseline`).
+
+--impl reference times the reference's own CPU integer path (digitize_torch + exact_linear_torch from its
+kernels.py, installed under baseline/_ref; the numpy restatement in oracle/ only if it is missing) on a bounded
+sample of the same workload with all host threads, and prints the same metric.
 """
 from __future__ import annotations
 
@@ -63,6 +68,10 @@ def gemm_bytes(M, K, N):
 # clocks sampled during the timed region
 # ------------------------------------------------------------------------------------------------------------------
 class ClockSampler:
+    """SM clock, power and throttle reasons during the timed region. Read-only NVML queries every 2 ms in a thread
+    (a decode step is ~1 ms, so nvidia-smi's 200 ms period would see a short timed region once at most); nvidia-smi
+    -lms 200 when NVML is not available. The GPU is found by the UUID torch reports, so CUDA_VISIBLE_DEVICES cannot
+    make it sample another GPU."""
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
@@ -71,8 +80,44 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.lines = []
+        self.nvml = None
+        self.stop = threading.Event()
+
+    def _nvml_open(self):
+        import pynvml as N
+        import torch
+        N.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.index).uuid)
+        uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        h = N.nvmlDeviceGetHandleByUUID(uuid)
+        return N, h
+
+    def _nvml_loop(self):
+        N, h = self.nvml
+        mx = N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM)
+        bits = [("hw_slowdown", N.nvmlClocksEventReasonHwSlowdown),
+                ("hw_thermal_slowdown", N.nvmlClocksEventReasonHwThermalSlowdown),
+                ("sw_thermal_slowdown", N.nvmlClocksEventReasonSwThermalSlowdown),
+                ("sw_power_cap", N.nvmlClocksEventReasonSwPowerCap)]
+        while not self.stop.is_set():
+            try:
+                sm = N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)
+                pw = N.nvmlDeviceGetPowerUsage(h) / 1000.0
+                r = N.nvmlDeviceGetCurrentClocksEventReasons(h)
+                flags = ["Active" if r & b else "Not Active" for _, b in bits]
+                self.lines.append(", ".join([str(sm), str(mx), f"{pw:.1f}", hex(r)] + flags))
+            except Exception:
+                pass
+            time.sleep(0.002)
 
     def __enter__(self):
+        try:
+            self.nvml = self._nvml_open()
+            self.t = threading.Thread(target=self._nvml_loop, daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
@@ -89,10 +134,13 @@ class ClockSampler:
 
     def wait_first_sample(self, timeout=5.0):
         t = time.time()
-        while self.proc is not None and not self.lines and time.time() - t < timeout:
+        while (self.proc is not None or self.nvml is not None) and not self.lines and time.time() - t < timeout:
             time.sleep(0.02)
 
     def __exit__(self, *a):
+        if self.nvml is not None:
+            self.stop.set()
+            self.t.join(timeout=2)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -100,10 +148,11 @@ class ClockSampler:
             except Exception:
                 self.proc.kill()
 
-    def summary(self):
+    def summary(self, since=0, until=None):
+        """Median SM clock, max clock and throttle reasons seen over the samples [since, until)."""
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[since:until]:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 8:
                 continue
@@ -116,7 +165,11 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvml every 2 ms" if self.nvml is not None else "nvidia-smi -lms 200"}
+
+    def mark(self):
+        """Index of the next sample (for summary(since, until))."""
+        return len(self.lines)
 
 
 # ------------------------------------------------------------------------------------------------------------------
@@ -211,11 +264,15 @@ def run_ours(args):
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+        c0 = clk.mark()
         with torch.cuda.stream(stream):
             t0.record()
             for _ in range(args.steps):
                 gA.replay()
             t1.record()
+        torch.cuda.synchronize()
+        c1 = clk.mark()
+        with torch.cuda.stream(stream):
             # per-GEMM durations from the last R steps of a second timed pass
             t2.record()
             for _ in range(max(args.steps // R, 1)):
@@ -259,7 +316,7 @@ def run_ours(args):
                      "kernel": "k_exact_tc_i8: algorithmic bytes of the 15 decode GEMM launches / their summed "
                                "event-timed durations (= per-launch average); traffic = ncu average per launch"},
         "sweep_decode": per_gemm,
-        "clocks": clk.summary(),
+        "clocks": clk.summary(c0, c1),
     }
     e2e = e2e_bench(dev, W, order, args)  # every rank: whole-job end-to-end rate, max time over ranks
     if world > 1:
@@ -275,7 +332,11 @@ def run_ours(args):
     result["sweep_tensor"] = tensor_sweep(dev, W, bf16_burst, args.quick)
     result["attention"] = attention_bench(dev, hbm, args.quick)
     if rank == 0:
+        # CPU leg: the oracle checks the timed step's outputs (as the checker), then the CPU baseline is timed
+        result["bitwise"] = bitwise_check(W, X, Y, order)
+        result["bitwise_ok"] = result["bitwise"]["ok"]
         if world == 1 and not args.quick:
+            result["ref_triton"] = ref_triton_decode(dev, W, hbm)
             del W, X, Y
             torch.cuda.empty_cache()
             result["decode_step"] = decode_step_bench(dev)
@@ -321,12 +382,36 @@ def _graph_time(fns, reps, stream, warm=2):
     return a.elapsed_time(b) / reps, per
 
 
+def int8_peak(dev, n=8192, reps=10):
+    """Dense INT8 tensor-core peak of this GPU, measured like the bf16 peak of MEASURED_PEAKS.json: torch._int_mm
+    (cuBLASLt, int8 x int8 -> int32) at n^3, 2 n^3 integer ops per call, best of `reps` single calls (burst)."""
+    import torch
+    a = torch.randint(-128, 128, (n, n), dtype=torch.int8, device=dev)
+    b = torch.randint(-128, 128, (n, n), dtype=torch.int8, device=dev)
+    for _ in range(3):
+        torch._int_mm(a, b)
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    del a, b
+    return 2.0 * n ** 3 / (best * 1e-3) / 1e12
+
+
 def tensor_sweep(dev, W, peak_bf16, quick):
-    """M in {256, 4096}: one graph per M with the five shapes in sequence (weights rotate through L2)."""
+    """M in {256, 4096}: one graph per M with the five shapes in sequence (weights rotate through L2). Executed
+    digit-product ops (6 M N K) against the measured bf16 dense peak and against the INT8 dense peak measured here
+    (the kernel runs INT8 MMAs, which B200 executes at twice the bf16 rate, so frac_i8_peak is its roofline)."""
     import torch
     from vllm_exact import kernels as KK
     stream = torch.cuda.Stream(dev)
-    out = {}
+    peak_i8 = int8_peak(dev)
+    out = {"int8_peak_TOPs": round(peak_i8, 1)}
     for M in TENSOR_M:
         if quick and M > 256:
             continue
@@ -338,9 +423,10 @@ def tensor_sweep(dev, W, peak_bf16, quick):
         _, per = _graph_time(fns, 3 if M > 256 else 10, stream)
         for (name, K, N), ms in zip(SHAPES, per):
             fl = 6.0 * M * N * K
-            out[f"{name}/M{M}"] = {"us": round(ms * 1e3, 1), "TFLOPs_executed": round(fl / ms / 1e9, 1),
+            out[f"{name}/M{M}"] = {"us": round(ms * 1e3, 1), "TOPs_executed": round(fl / ms / 1e9, 1),
+                                   "frac_i8_peak": round(fl / ms / 1e9 / peak_i8, 3),
                                    "frac_bf16_peak": round(fl / ms / 1e9 / peak_bf16, 3),
-                                   "TFLOPs_useful": round(fl / 3 / ms / 1e9, 1)}
+                                   "TOPs_useful": round(fl / 3 / ms / 1e9, 1)}
         del xs, ys
     return out
 
@@ -547,34 +633,68 @@ def decode_step_bench(dev, quick=False):
     return res
 
 
-class CpuSample:
-    """The reference's CPU integer path, restated in oracle/ (numpy; integer dot products as exact float64 BLAS
-    products), on a bounded sample of the decode sweep. A step is one (M, shape) GEMM of the headline order, taken in
-    turn, with its output columns capped at `ncap` (output columns are independent, so a capped GEMM is a faithful
-    sample). Weights are digitized once before timing, as the plugin does at load; a timed step digitizes its
-    activations, runs the exact integer GEMM and rounds the output to bf16, as the GPU step does. Metric: algorithmic
-    bytes of the sampled GEMMs / time."""
+def _reference_kernels():
+    """The reference's own kernels.py (installed, git-ignored, under baseline/_ref), whose CPU functions
+    digitize_torch / exact_linear_torch (kernels.py:22-39, :89-100) are its stock CPU integer path; None when the
+    reference is not installed."""
+    try:
+        return _load_reference_module("kernels")
+    except SystemExit:
+        return None
 
-    def __init__(self, ncap):
-        import numpy as np
-        from oracle import exact_oracle as O
-        self.np, self.O, self.ncap = np, O, ncap
-        rng = np.random.default_rng(0)
+
+class CpuSample:
+    """The reference's CPU integer path on a bounded sample of the decode sweep. A step is one (M, shape) GEMM of the
+    headline order, taken in turn, with its output columns capped at `ncap` (output columns are independent, so a
+    capped GEMM is a faithful sample). Weights are digitized once before timing, as the plugin does at load; a timed
+    step digitizes its activations, runs the exact integer GEMM and rounds the output to bf16, as the GPU step does.
+    backend "reference": the reference's own digitize_torch + exact_linear_torch + .bfloat16() on CPU tensors with all
+    host threads; "port": the numpy restatement in oracle/ (used only when the reference is not installed). Inputs
+    follow the sweep's distributions. Metric: algorithmic bytes of the sampled GEMMs / time."""
+
+    def __init__(self, ncap, backend="reference"):
+        import torch
+        self.torch, self.ncap = torch, ncap
+        self.RK = _reference_kernels() if backend == "reference" else None
+        self.kind = "reference" if self.RK is not None else "port"
+        if self.kind == "port":
+            from oracle import exact_oracle as O
+            self.O = O
+        torch.set_num_threads(os.cpu_count())
         self.order = [(M, name, K, N) for M in DECODE_M for name, K, N in SHAPES]
-        self.wd = {name: O.digitize(rng.standard_normal((min(N, ncap), K), dtype=np.float32) * 0.02, 14)
-                   for name, K, N in SHAPES}
-        self.x = {(M, name): rng.standard_normal((M, K), dtype=np.float32) for M, name, K, N in self.order}
+        g = torch.Generator().manual_seed(0)
+        self.wd, self.x = {}, {}
+        for name, K, N in SHAPES:
+            w = (torch.randn(min(N, ncap), K, generator=g) * 0.02).bfloat16().float()
+            self.wd[name] = self._digitize(w)
+        for M, name, K, N in self.order:
+            x = torch.randn(M, K, generator=g)
+            x[torch.rand(M, K, generator=g) < 0.001] *= 50
+            self.x[(M, name)] = x.bfloat16().float()
         self.i = 0
+
+    def _digitize(self, x):
+        if self.kind == "reference":
+            return self.RK.digitize_torch(x, 14)
+        return self.O.digitize(x.numpy(), 14)
+
+    def _linear_bf16(self, xd, wd):
+        if self.kind == "reference":
+            return self.RK.exact_linear_torch(xd, wd, 14, True).bfloat16()
+        return self.O.f32_to_bf16_bits(self.O.exact_linear(xd, wd, 14, True))
 
     def step(self):
         """Run the next GEMM of the order; return (algorithmic bytes, seconds)."""
         M, name, K, N = self.order[self.i % len(self.order)]
         self.i += 1
-        O = self.O
         t = time.perf_counter()
-        y = O.exact_linear(O.digitize(self.x[(M, name)], 14), self.wd[name], 14, True)
-        O.f32_to_bf16_bits(y)
+        self._linear_bf16(self._digitize(self.x[(M, name)]), self.wd[name])
         return gemm_bytes(M, K, min(N, self.ncap)), time.perf_counter() - t
+
+    def threads(self):
+        if self.kind == "reference":
+            return self.torch.get_num_threads()
+        return _blas_threads()
 
 
 def _blas_threads():
@@ -588,10 +708,10 @@ def _blas_threads():
         return int(os.environ.get("OMP_NUM_THREADS", os.cpu_count()))
 
 
-def cpu_baseline(budget_s=20.0, ncap=2048):
+def cpu_baseline(budget_s=20.0, ncap=1024):
     """CPU baseline beside the GPU arm's line: whole passes over the 15 sampled GEMMs until `budget_s` (at most 3)."""
-    threads = _blas_threads()
     smp = CpuSample(ncap)
+    threads = smp.threads()
     tot_bytes, tot_s, passes = 0, 0.0, 0
     while tot_s < budget_s and passes < 3:
         for _ in smp.order:
@@ -599,28 +719,62 @@ def cpu_baseline(budget_s=20.0, ncap=2048):
             tot_bytes += b
             tot_s += dt
         passes += 1
-    return {"value": round(tot_bytes / tot_s / 1e12, 6), "unit": "TB/s", "cores": threads, "kind": "port",
+    src = ("the reference's digitize_torch + exact_linear_torch + bf16 (its kernels.py, on CPU tensors)"
+           if smp.kind == "reference" else "the numpy restatement in oracle/ (reference not installed)")
+    return {"value": round(tot_bytes / tot_s / 1e12, 7), "unit": "TB/s", "cores": threads, "kind": smp.kind,
             "sample": f"{passes} pass(es) of the 15 decode GEMMs with N capped at {ncap} output columns (activation "
-                      f"digitize + exact integer GEMM + bf16; weights digitized before timing), numpy oracle, "
-                      f"{threads} host threads",
+                      f"digitize + exact integer GEMM + bf16; weights digitized before timing), {src}, {threads} host "
+                      f"threads",
             "seconds": round(tot_s, 2)}
 
 
+def bitwise_check(W, X, Y, order, rows_of=lambda M: sorted({0, M - 1}), chunk=16384):
+    """Bit check of the GPU outputs of the timed step against the CPU oracle (the checker; nothing here is timed):
+    for every GEMM of `order`, the rows rows_of(M) of the bf16 activations are digitized on the CPU and multiplied
+    exactly with the weight digits (all N output columns, in column chunks), and the bf16 results must equal the GPU's
+    output rows bit for bit. Rows are independent (the reference's tests/test_reference_cpu.py:37-46), so a row
+    sample is a faithful check of the kernels at these exact grid shapes."""
+    import numpy as np
+    import torch
+    from oracle import exact_oracle as O
+    _blas_threads()
+    checked, bad, first_bad = 0, 0, None
+    for M, name, K, N in order:
+        rows = rows_of(M)
+        x = X[(M, name)][rows].float().cpu().numpy()
+        xd = O.digitize(x, 14)
+        y = Y[(M, name)][rows].cpu().view(torch.int16).numpy().view(np.uint16)
+        wh, wl, cw, sw = W[name]
+        for c0 in range(0, N, chunk):
+            c1 = min(N, c0 + chunk)
+            wd = [t[c0:c1].cpu().numpy() for t in (wh, wl, cw, sw)]
+            ref = O.f32_to_bf16_bits(O.exact_linear(xd, wd, 14, True))
+            nbad = int((ref != y[:, c0:c1]).sum())
+            checked += ref.size
+            if nbad and first_bad is None:
+                first_bad = f"{name}/M{M} columns {c0}:{c1}"
+            bad += nbad
+    return {"ok": bad == 0, "elements": checked, "mismatches": bad, "first_mismatch": first_bad,
+            "sample": "rows {0, M-1} of each of the 15 GEMMs of the timed step x all N output columns vs the CPU "
+                      "oracle (bf16 bits)"}
+
+
 def run_reference(args):
-    """The reference arm: W untimed warm-up steps, then exactly K timed steps of CpuSample, on rank 0 only (the other
-    ranks of a torchrun launch exit at once). The output-column cap is sized from the warm-up so that the K + W steps
-    take about two minutes in all (at most 2048 columns, at least 16)."""
+    """The reference arm: W untimed warm-up steps, then exactly K timed steps of CpuSample (the reference's own CPU
+    path from baseline/_ref), on rank 0 only (the other ranks of a torchrun launch exit at once). The output-column
+    cap is sized from a probe so that the K + W steps take about two minutes in all (at most 2048 columns, at
+    least 16)."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     os.environ["OMP_NUM_THREADS"] = os.environ["OPENBLAS_NUM_THREADS"] = str(os.cpu_count())  # before numpy loads
-    threads = _blas_threads()
     target = 120.0 / (args.steps + args.warmup)  # seconds per step
     probe = CpuSample(256)
     costs = [probe.step()[1] for _ in probe.order]  # one pass at 256 columns: the slowest GEMM bounds a step
     ncap = int(max(16, min(2048, 256 * target / max(max(costs), 1e-6))) // 16 * 16)
     smp = CpuSample(ncap)
+    threads = smp.threads()
     for _ in range(args.warmup):
         smp.step()
     tot_bytes, tot_s = 0, 0.0
@@ -628,18 +782,22 @@ def run_reference(args):
         b, dt = smp.step()
         tot_bytes += b
         tot_s += dt
-    v = round(tot_bytes / tot_s / 1e12, 6)
+    v = round(tot_bytes / tot_s / 1e12, 7)
+    src = ("the reference's own digitize_torch + exact_linear_torch + .bfloat16() (src/vllm_exact/kernels.py:22-39, "
+           ":89-100, installed under baseline/_ref) on CPU tensors" if smp.kind == "reference" else
+           "the numpy restatement in oracle/ (the reference is not installed)")
     sample = (f"{args.steps} timed steps after {args.warmup} warm-up steps; a step is one of the 15 decode GEMMs in "
               f"turn with N capped at {ncap} output columns (activation digitize + exact integer GEMM + bf16; weights "
-              f"digitized before timing), numpy oracle, {threads} host threads")
+              f"digitized before timing), {src}, {threads} host threads")
     step_bytes = sum(gemm_bytes(M, K, N) for M in DECODE_M for name, K, N in SHAPES)
     print(json.dumps({
         "metric": METRIC, "value": v, "unit": "TB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(tot_s / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int64 (CPU)", "data": "synthetic", "impl": "reference",
-        "config": {"workload": WORKLOAD, "parallelism": "cpu", "sample": sample, "per_step_bytes": tot_bytes // args.steps,
+        "config": {"workload": WORKLOAD + f"; CPU sample: output columns capped at {ncap} per GEMM",
+                   "parallelism": "cpu", "sample": sample, "per_step_bytes": tot_bytes // args.steps,
                    "full_step_ms_at_sampled_rate": round(step_bytes / (v * 1e12) * 1e3, 1)},
-        "cpu_baseline": {"value": v, "unit": "TB/s", "cores": threads, "kind": "port", "sample": sample,
+        "cpu_baseline": {"value": v, "unit": "TB/s", "cores": threads, "kind": smp.kind, "sample": sample,
                          "seconds": round(tot_s, 2)},
         "e2e": {"value": v, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -831,7 +989,7 @@ def run_case(args):
     kind, *rest = args.case.split(":")
     if kind == "gemm":
         name, M = rest[0], int(rest[1])
-        algo = {"tc_i8": KK.EX_ALGO_TC_I8, "tc_pair": KK.EX_ALGO_TC_I8_PAIR, "simt": KK.EX_ALGO_SIMT,
+        algo = {"tc_i8": KK.EX_ALGO_TC_I8, "simt": KK.EX_ALGO_SIMT,
                 "auto": KK.EX_ALGO_AUTO}[rest[2] if len(rest) > 2 else "auto"]
         (K, N), = [(k, n) for nm, k, n in SHAPES if nm == name]
         W = make_weight_digits(K, N, 1, dev)
@@ -884,6 +1042,73 @@ def _load_reference_module(name):
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
     return mod
+
+
+# Tile configurations of the reference's shipped B300 tuning table (src/vllm_exact/cfg_table_b300_F14.json) for
+# M = 1, 16 and 64, and its defaults (src/vllm_exact/plugin.py:_cfg), as (BM, BN, BK, warps, stages, GM, split_k).
+REF_DECODE_CFGS = {1: [(16, 64, 256, 4, 3, 8, 4), (16, 128, 128, 4, 4, 8, 4), (16, 128, 128, 4, 4, 8, 2),
+                       (16, 128, 128, 4, 4, 8, 1)],
+                   16: [(16, 64, 256, 4, 3, 8, 4), (16, 128, 128, 4, 4, 8, 4), (16, 128, 128, 4, 4, 8, 2),
+                        (16, 128, 128, 4, 4, 8, 1)],
+                   64: [(64, 64, 128, 4, 3, 8, 4), (64, 64, 128, 4, 3, 8, 2), (64, 64, 128, 4, 3, 8, 1),
+                        (16, 64, 256, 4, 3, 8, 4), (64, 128, 128, 4, 4, 8, 1)]}
+
+
+def ref_triton_decode(dev, W, hbm, budget_s=150.0):
+    """The reference's own Triton exact GEMM (kernels.py:_exact_kernel / _exact_bf16_kernel + _exact_fin, from
+    baseline/_ref) against ours on the same B200 and the same digits, at the headline decode shapes. Both arms are
+    timed the same way: one CUDA graph per M holding the five GEMMs with timing events around each (weights rotate
+    through L2, so every GEMM streams its weights from HBM). For every shape the reference gets the best of its
+    B300-table and default tile configurations for that M, each with INT8 and with bf16 MMAs; each reference output is
+    also compared bitwise with ours. Stops adding candidates after `budget_s` seconds (Triton compiles each one)."""
+    import torch
+    from vllm_exact import kernels as KK
+    try:
+        RK = _load_reference_module("kernels")
+    except SystemExit as e:
+        return {"unavailable": str(e)}
+    t_start = time.time()
+    stream = torch.cuda.Stream(dev)
+    res = {}
+    for M in DECODE_M:
+        xs = {name: KK.digitize(make_activation(M, K, 17 * M + i, dev), 14) for i, (name, K, N) in enumerate(SHAPES)}
+        ours_y = {name: torch.empty(M, N, device=dev, dtype=torch.bfloat16) for name, K, N in SHAPES}
+        KK.reserve_workspace(max(KK.lib().ex_linear_workspace_bytes(M, N, K, 0, 0) for _, K, N in SHAPES), dev,
+                             stream=stream)
+        fns = [(lambda n=name: KK.exact_linear(xs[n], W[n], 14, True, out=ours_y[n])) for name, K, N in SHAPES]
+        _, ours_ms = _graph_time(fns, 10, stream)
+        best = {}
+        for cfg in REF_DECODE_CFGS[M]:
+            for mma in (0, 1):
+                if time.time() - t_start > budget_s and best:
+                    break
+                c = cfg + (mma,)
+                ys = {name: torch.empty(M, N, device=dev, dtype=torch.bfloat16) for name, K, N in SHAPES}
+                rf = [(lambda n=name, c=c: RK.exact_linear(xs[n], W[n], 14, True, out=ys[n], cfg=c))
+                      for name, K, N in SHAPES]
+                try:
+                    _, ref_ms = _graph_time(rf, 5, stream)
+                except Exception as e:  # a configuration that does not compile here
+                    print(f"reference cfg {c} failed: {type(e).__name__}", file=sys.stderr)
+                    continue
+                for (name, K, N), ms in zip(SHAPES, ref_ms):
+                    same = bool(torch.equal(ys[name], ours_y[name]))
+                    prev = best.get(name)
+                    if prev is None or ms < prev[0]:
+                        best[name] = (ms, c, same and (prev is None or prev[2]))
+                    elif not same:
+                        best[name] = (prev[0], prev[1], False)
+        for (name, K, N), ms in zip(SHAPES, ours_ms):
+            if name not in best:
+                continue
+            rms, rc, same = best[name]
+            by = gemm_bytes(M, K, N)
+            res[f"{name}/M{M}"] = {"ours_us": round(ms * 1e3, 2), "ref_us": round(rms * 1e3, 2),
+                                   "speedup": round(rms / ms, 3), "ours_frac_hbm": round(by / ms / 1e6 / hbm, 3),
+                                   "ref_frac_hbm": round(by / rms / 1e6 / hbm, 3), "ref_cfg": list(rc),
+                                   "bitwise_equal": same}
+        del xs, ours_y
+    return res
 
 
 def run_ref_triton(args):

@@ -40,13 +40,11 @@ enum {
 /* element types */
 enum { EX_DTYPE_F32 = 0, EX_DTYPE_BF16 = 1, EX_DTYPE_F16 = 2 };
 
-/* exact GEMM algorithms; all produce bit-identical results */
+/* exact GEMM algorithms; all produce bit-identical results (other values are rejected with EX_ERR_ARG) */
 enum {
-  EX_ALGO_AUTO = 0,    /* pick by shape */
-  EX_ALGO_SIMT = 1,    /* CUDA cores, int8 dp4a, int32 accumulation */
-  EX_ALGO_TC_I8 = 2,   /* tcgen05 kind::i8 tensor cores, TMA-fed, int32 accumulators in tensor memory */
-  EX_ALGO_TC_BF16 = 3, /* tcgen05 kind::f16 tensor cores on bf16-converted digits, fp32 accumulators drained to int */
-  EX_ALGO_TC_I8_PAIR = 4 /* tcgen05 kind::i8 on CTA pairs (cta_group::2, 256 weight rows x 128 tokens per pair tile) */
+  EX_ALGO_AUTO = 0,  /* pick by shape and alignment */
+  EX_ALGO_SIMT = 1,  /* CUDA cores, int8 dp4a, int32 accumulation; any alignment */
+  EX_ALGO_TC_I8 = 2  /* tcgen05 kind::i8 tensor cores, TMA-fed, int32 accumulators in tensor memory */
 };
 
 const char* ex_version(void);
@@ -54,8 +52,11 @@ const char* ex_status_string(int status);
 /* Message of the last EX_ERR_CUDA on this host thread. */
 const char* ex_last_error_string(void);
 
-/* Synchronizes the current device, stores the device error word into *code (0 = none) and clears it.
- * Returns EX_OK, or EX_ERR_CUDA if the synchronize failed. For tests and diagnostics, not for hot paths. */
+/* Synchronizes the current device, stores the device error word into *code (0 = none) and clears it. When the
+ * code is non-zero it also clears the static scratch of ex_linear_noalloc on every device that has used it, since
+ * a call stopped by a timed-out wait may have left partial sums there (caller-owned split-K workspaces of ex_linear
+ * must then be re-zeroed by their owner). Returns EX_OK, or EX_ERR_CUDA if a CUDA call failed. For tests and
+ * diagnostics, not for hot paths. */
 int ex_device_error(int* code);
 
 /*
@@ -128,6 +129,15 @@ int ex_linear_noalloc(const int8_t* xh, const int8_t* xl, int64_t ldx, const int
                       const int8_t* wh, const int8_t* wl, int64_t ldw, const int32_t* cw, const int32_t* sw,
                       int64_t M, int64_t N, int64_t K, int F, int trunc, void* out, int out_dtype, int64_t ldo,
                       int split_k, int algo, void* stream);
+
+/* Clears the static scratch of ex_linear_noalloc on the current device, ordered on `stream`. Needed only after a
+ * device error (a call stopped by a timed-out wait can leave partial sums in it); ex_device_error() already does
+ * this when it reports an error. No counterpart in the reference. */
+int ex_linear_noalloc_reset(void* stream);
+
+/* Diagnostics for tests of the recovery path: fills the static scratch of the current device with `byte_value`
+ * (0..255) on `stream`, which stands for what a stopped call can leave behind. Never needed in normal use. */
+int ex_linear_noalloc_fill_scratch(int byte_value, void* stream);
 
 /*
  * Integer part of ex_linear without the scaling epilogue: tot (M x N int64, ld ldt) = the exact integer total

@@ -1,7 +1,7 @@
 // Host check of the tensor-core exact GEMM's work plan (vllm-exact_b200/csrc/ex_tc_plan.h: tc_plan, TcWalk,
 // tc_split_slot), compiled with g++ by tests/test_planner_host.py. No GPU is involved: the kernel's bit-exactness
 // under every partition rests on these properties, checked here for every plan of the shape matrix below:
-//   * the grid is groups x gs CTAs (x 2 for CTA pairs), and both CTAs of a pair walk identical segments;
+//   * the grid is groups x gs CTAs;
 //   * every segment lies inside the tile grid, with 0 <= kb < ke <= KI;
 //   * every (m-tile, n-tile) has its K iterations [0, KI) covered exactly once (so each ticket reaches KI once);
 //   * a tile covered by more than one segment (a split tile) gets one workspace slot from all of its contributors,
@@ -22,11 +22,11 @@ struct Fail {
   char msg[512];
 };
 
-bool check_plan(int64_t M, int64_t N, int64_t K, int split_k, int algo, int sms, long long& nseg, Fail& f) {
-  const TcPlan p = tc_plan(M, N, K, split_k, algo, sms);
+bool check_plan(int64_t M, int64_t N, int64_t K, int split_k, int sms, long long& nseg, Fail& f) {
+  const TcPlan p = tc_plan(M, N, K, split_k, sms);
   auto bad = [&](const char* what) {
-    std::snprintf(f.msg, sizeof f.msg, "M=%lld N=%lld K=%lld split=%d algo=%d sms=%d: %s", (long long)M,
-                  (long long)N, (long long)K, split_k, algo, sms, what);
+    std::snprintf(f.msg, sizeof f.msg, "M=%lld N=%lld K=%lld split=%d sms=%d: %s", (long long)M, (long long)N,
+                  (long long)K, split_k, sms, what);
     return false;
   };
   TcArgs a{};
@@ -34,10 +34,9 @@ bool check_plan(int64_t M, int64_t N, int64_t K, int split_k, int algo, int sms,
   a.N = (int)N;
   a.K = (int)K;
   tc_plan_args(p, a);
-  const int halves = p.pair ? 2 : 1;
-  if (p.groups < 1 || p.gs < 1 || p.G != p.groups * p.gs * halves) return bad("grid size");
+  if (p.groups < 1 || p.gs < 1 || p.G != p.groups * p.gs) return bad("grid size");
   if (p.m_tiles != (int)((M + p.BT - 1) / p.BT) || (int64_t)p.m_tiles * p.BT < M) return bad("m-tiles");
-  if ((int64_t)p.n_tiles * (p.pair ? 256 : 128) < N || (int64_t)p.KI * TC_BK < K) return bad("n-tiles / KI");
+  if ((int64_t)p.n_tiles * 128 < N || (int64_t)p.KI * TC_BK < K) return bad("n-tiles / KI");
   if (p.stages < 2 || p.smem > 227 * 1024) return bad("shared memory");
   const size_t tiles = (size_t)p.m_tiles * p.n_tiles;
   std::vector<std::vector<std::pair<int, int>>> cov(tiles);
@@ -46,18 +45,6 @@ bool check_plan(int64_t M, int64_t N, int64_t K, int split_k, int algo, int sms,
   for (int cta = 0; cta < p.G; ++cta) {
     TcWalk w(a, cta);
     TcSeg s;
-    if (p.pair && (cta & 1)) {  // the odd CTA of a pair: same segments as its even partner
-      TcWalk w0(a, cta - 1);
-      TcSeg s0;
-      for (;;) {
-        const bool g1 = w.next(s), g0 = w0.next(s0);
-        if (g1 != g0) return bad("pair walks differ in length");
-        if (!g1) break;
-        if (s.m_tile != s0.m_tile || s.n_tile != s0.n_tile || s.kb != s0.kb || s.ke != s0.ke)
-          return bad("pair walks differ");
-      }
-      continue;
-    }
     while (w.next(s)) {
       ++nseg;
       if (s.m_tile < 0 || s.m_tile >= p.m_tiles || s.n_tile < 0 || s.n_tile >= p.n_tiles) return bad("tile range");
@@ -70,8 +57,8 @@ bool check_plan(int64_t M, int64_t N, int64_t K, int split_k, int algo, int sms,
       if (slot_of[t] < 0) slot_of[t] = sl;
       else if (slot_of[t] != sl) return bad("contributors of a split tile disagree on its slot");
       if (p.ws_bytes == 0) return bad("split tile in a plan without workspace");
-      const size_t acc_end = p.cnt_bytes + (size_t)(sl * halves + halves) * p.BT * 128 * 8;
-      if (acc_end > p.ws_bytes || (size_t)(sl * halves + halves) * 4 > p.cnt_bytes) return bad("slot outside workspace");
+      const size_t acc_end = p.cnt_bytes + (size_t)(sl + 1) * p.BT * 128 * 8;
+      if (acc_end > p.ws_bytes || (size_t)(sl + 1) * 4 > p.cnt_bytes) return bad("slot outside workspace");
     }
   }
   std::vector<long long> used;
@@ -103,7 +90,6 @@ int main() {
   const int64_t Ns[] = {1, 100, 128, 129, 1024, 4096, 6144, 24576, 151936};
   const int64_t Ks[] = {1, 100, 128, 1024, 4096, 12288, 65536};
   const int splits[] = {0, 1, 2, 3, 4, 8};
-  const int algos[] = {EX_ALGO_TC_I8, EX_ALGO_TC_I8_PAIR};
   const int smss[] = {148, 132, 7, 2, 1};
   long long plans = 0, nseg = 0;
   Fail f;
@@ -111,14 +97,13 @@ int main() {
     for (int64_t N : Ns)
       for (int64_t K : Ks)
         for (int sk : splits)
-          for (int algo : algos)
-            for (int sms : smss) {
-              ++plans;
-              if (!check_plan(M, N, K, sk, algo, sms, nseg, f)) {
-                std::printf("FAIL %s\n", f.msg);
-                return 1;
-              }
+          for (int sms : smss) {
+            ++plans;
+            if (!check_plan(M, N, K, sk, sms, nseg, f)) {
+              std::printf("FAIL %s\n", f.msg);
+              return 1;
             }
+          }
   std::printf("OK %lld %lld\n", plans, nseg);
   return 0;
 }

@@ -95,13 +95,14 @@ def test_argument_validation_without_gpu(L):
 
 def test_exact_cfgs_parse():
     """Every autotuning candidate is a configuration exact_linear accepts (algorithm, split-K), and reference-style
-    tuples keep their meaning (split-K at index 6, MMA kind at index 7)."""
+    tuples keep their meaning (split-K at index 6; either MMA kind at index 7 selects the INT8 tensor cores)."""
     from vllm_exact import kernels as K
     seen = {K._parse_cfg(c) for c in K.EXACT_CFGS}
     assert len(seen) == len(K.EXACT_CFGS)
-    assert all(a in (K.EX_ALGO_TC_I8, K.EX_ALGO_TC_I8_PAIR, K.EX_ALGO_SIMT) and sk >= 0 for a, sk in seen)
+    assert all(a in (K.EX_ALGO_TC_I8, K.EX_ALGO_SIMT) and sk >= 0 for a, sk in seen)
     assert K._parse_cfg(None) == (K.EX_ALGO_AUTO, 0)
     assert K._parse_cfg((64, 128, 128, 4, 4, 8, 4, 0)) == (K.EX_ALGO_TC_I8, 4)
+    assert K._parse_cfg((64, 128, 128, 4, 4, 8, 2, 1)) == (K.EX_ALGO_TC_I8, 2)  # bf16-MMA request: same bits
 
 
 def test_header_is_plain_c_and_links(tmp_path):

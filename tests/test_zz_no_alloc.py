@@ -72,6 +72,34 @@ def test_noalloc_matches_workspace_entry_point(env, M, N, Kd, algo, split_k):
     assert lib.device_error() == 0
 
 
+def test_noalloc_recovers_from_dirty_scratch(env):
+    """A call stopped by a timed-out wait can leave split-K partials and tickets in the shared scratch, which would
+    make every later call wrong. Stand in for that by filling the scratch with non-zero bytes (no GPU fault is
+    involved: the kernels never wait on a ticket, so dirty tickets only leave split tiles unfinished), check that a
+    call then goes wrong, and that ex_linear_noalloc_reset brings back the exact bits on two calls in a row."""
+    lib, K = env
+    L = lib.lib()
+    M, N, Kd = 64, 4096, 4096  # the automatic tensor-core plan splits every tile four ways: scratch in use
+    assert L.ex_linear_workspace_bytes(M, N, Kd, 0, lib.EX_ALGO_TC_I8) > 0
+    xd, wd = _inputs(K, M, N, Kd, seed=7)
+    ref = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    assert _with_workspace(L, xd, wd, ref) == lib.EX_OK
+    st = torch.cuda.current_stream().cuda_stream
+    assert L.ex_linear_noalloc_fill_scratch(0x5A, st) == lib.EX_OK
+    out = torch.full((M, N), float("nan"), device=DEV, dtype=torch.bfloat16)
+    assert _noalloc(L, xd, wd, out) == lib.EX_OK
+    torch.cuda.synchronize()
+    assert not torch.equal(out, ref)  # dirty tickets: split tiles are never finished
+    assert L.ex_linear_noalloc_reset(st) == lib.EX_OK
+    for _ in range(2):
+        out = torch.full((M, N), float("nan"), device=DEV, dtype=torch.bfloat16)
+        assert _noalloc(L, xd, wd, out) == lib.EX_OK
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+    assert L.ex_linear_noalloc_fill_scratch(256, st) == lib.EX_ERR_ARG
+    assert lib.device_error() == 0
+
+
 def test_noalloc_refuses_oversized_plan(env):
     """A SIMT split-K plan for M=1024, N=4096 needs 32 MiB of int64 partials, more than the static scratch."""
     lib, K = env

@@ -152,10 +152,9 @@ int linear_impl(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* 
     return cuda_status(launch_simt<PARTIAL>(F, trunc, out_dtype, xh, xl, ldx, cx, sx, wh, wl, ldw, cw, sw, (int)M,
                                             (int)N, (int)K, p, out, ldo, workspace, st));
   }
-  if (algo == EX_ALGO_TC_BF16) return EX_ERR_UNSUPPORTED;
-  if (algo == EX_ALGO_TC_I8 || algo == EX_ALGO_TC_I8_PAIR) {
+  if (algo == EX_ALGO_TC_I8) {
     if (!ex::tc_supported(xh, xl, ldx, wh, wl, ldw, M, N, K)) return EX_ERR_ALIGN;
-    const ex::TcPlan p = ex::tc_plan(M, N, K, split_k, algo, num_sms());
+    const ex::TcPlan p = ex::tc_plan(M, N, K, split_k, num_sms());
     if (p.ws_bytes > 0 && (!workspace || workspace_bytes < p.ws_bytes)) return EX_ERR_WORKSPACE;
     if (p.ws_bytes > 0 && reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return EX_ERR_ALIGN;
     cudaError_t e = ex::launch_tc<PARTIAL>(p, F, trunc, out_dtype, xh, xl, ldx, cx, sx, wh, wl, ldw, cw, sw, (int)M,
@@ -186,6 +185,25 @@ int noalloc_scratch(cudaStream_t st, void** out) {
   }
   *out = g_noalloc_ptr[dev];
   return EX_OK;
+}
+
+// Clears the scratch of every device that has used it (synchronously, each with its own device current). A call
+// that stopped early on a timed-out wait can leave split-K partials and tickets behind; ex_device_error() calls this
+// whenever it reports such an error, so later calls start from zero again.
+int noalloc_clear_all() {
+  int cur = 0;
+  cudaError_t e = cudaGetDevice(&cur);
+  if (e != cudaSuccess) return cuda_status(e);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  int rc = EX_OK;
+  for (int d = 0; d < 128; ++d) {
+    if (!g_noalloc_ptr[d]) continue;
+    if ((e = cudaSetDevice(d)) == cudaSuccess) e = cudaMemset(g_noalloc_ptr[d], 0, EX_NOALLOC_SCRATCH_BYTES);
+    if (e != cudaSuccess && rc == EX_OK) rc = cuda_status(e);
+  }
+  e = cudaSetDevice(cur);
+  if (e != cudaSuccess && rc == EX_OK) rc = cuda_status(e);
+  return rc;
 }
 
 // 4-D tensor map over a paged K or V cache: (head dim, KV head, offset in page, page), 16-token x 64-dim boxes.
@@ -225,11 +243,9 @@ size_t linear_ws(int64_t M, int64_t N, int64_t K, int split_k, int algo) {
   if (M <= 0 || N <= 0) return 0;
   size_t a = simt_plan(M, N, K, split_k).ws_bytes;
   if (algo == EX_ALGO_SIMT) return a;
-  if (algo != EX_ALGO_AUTO) return std::max(a, ex::tc_plan(M, N, K, split_k, algo, num_sms()).ws_bytes);
-  // automatic choice: enough for whichever tensor-core plan it may pick
-  const size_t b = ex::tc_plan(M, N, K, split_k, EX_ALGO_TC_I8, num_sms()).ws_bytes;
-  const size_t c = ex::tc_plan(M, N, K, split_k, EX_ALGO_TC_I8_PAIR, num_sms()).ws_bytes;
-  return std::max(a, std::max(b, c));
+  const size_t b = ex::tc_plan(M, N, K, split_k, num_sms()).ws_bytes;
+  if (algo == EX_ALGO_TC_I8) return b;
+  return std::max(a, b);  // automatic choice: enough for either algorithm
 }
 
 }  // namespace
@@ -265,6 +281,7 @@ int ex_device_error(int* code) {
   e = cudaMemcpyToSymbol(g_ex_dev_error, &zero, sizeof(int));
   if (e != cudaSuccess) return cuda_status(e);
   *code = v;
+  if (v != 0) return noalloc_clear_all();  // a stopped call may have left the static split-K scratch dirty
   return EX_OK;
 }
 
@@ -325,9 +342,8 @@ int ex_linear_noalloc(const int8_t* xh, const int8_t* xl, int64_t ldx, const int
   size_t need = 0;
   if (chosen == EX_ALGO_SIMT)
     need = simt_plan(M, N, K, split_k).ws_bytes;
-  else if ((chosen == EX_ALGO_TC_I8 || chosen == EX_ALGO_TC_I8_PAIR) &&
-           ex::tc_supported(xh, xl, ldx, wh, wl, ldw, M, N, K))
-    need = ex::tc_plan(M, N, K, split_k, chosen, num_sms()).ws_bytes;
+  else if (chosen == EX_ALGO_TC_I8 && ex::tc_supported(xh, xl, ldx, wh, wl, ldw, M, N, K))
+    need = ex::tc_plan(M, N, K, split_k, num_sms()).ws_bytes;
   if (need > EX_NOALLOC_SCRATCH_BYTES) {
     g_last_error = "ex_linear_noalloc: this shape's split-K plan needs " + std::to_string(need) +
                    " bytes of scratch, more than the static EX_NOALLOC_SCRATCH_BYTES (" +
@@ -339,6 +355,21 @@ int ex_linear_noalloc(const int8_t* xh, const int8_t* xl, int64_t ldx, const int
   if (rc != EX_OK) return rc;
   return linear_impl<false>(xh, xl, ldx, cx, sx, wh, wl, ldw, cw, sw, M, N, K, F, trunc, out, out_dtype, ldo, scratch,
                             EX_NOALLOC_SCRATCH_BYTES, split_k, algo, (cudaStream_t)stream);
+}
+
+int ex_linear_noalloc_reset(void* stream) {
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch((cudaStream_t)stream, &scratch);
+  if (rc != EX_OK) return rc;
+  return cuda_status(cudaMemsetAsync(scratch, 0, EX_NOALLOC_SCRATCH_BYTES, (cudaStream_t)stream));
+}
+
+int ex_linear_noalloc_fill_scratch(int byte_value, void* stream) {
+  if (byte_value < 0 || byte_value > 255) return EX_ERR_ARG;
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch((cudaStream_t)stream, &scratch);
+  if (rc != EX_OK) return rc;
+  return cuda_status(cudaMemsetAsync(scratch, byte_value, EX_NOALLOC_SCRATCH_BYTES, (cudaStream_t)stream));
 }
 
 int ex_linear_partial_i64(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* cx, const int8_t* wh,

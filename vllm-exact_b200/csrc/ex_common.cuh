@@ -126,8 +126,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int co
 
 // ------------------------------------------------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor), tiled 2D loads into this CTA's shared memory, completion counted on an mbarrier.
-// Every tensor load of this library writes only the issuing CTA's shared memory (no multicast form is used); the
-// CTA-pair form below only lets the completion count on the pair's even CTA's barrier.
+// Every tensor load of this library writes only the issuing CTA's shared memory (no multicast form is used).
 // ------------------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             uint64_t cache_hint) {
@@ -203,17 +202,6 @@ __device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t a_desc, uint
       : "memory");
 }
 
-// D[tmem] (+)= A[smem] * B[smem]^T, bf16 x bf16 -> fp32, both operands K-major.
-__device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
 // 32 lanes x 32 bit, 16 consecutive columns per thread (thread i of the warp reads TMEM lane base+i).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
@@ -229,76 +217,6 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
                : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// ------------------------------------------------------------------------------------------------------------------
-// CTA pairs (cluster of 2, tcgen05 cta_group::2): one MMA spans the tensor cores of both SMs; operand A's rows and
-// operand B's columns are split between the two CTAs' shared memories (same offsets), and each CTA's TMEM holds the
-// accumulator rows of its half of A. The even CTA of the pair issues the MMAs.
-// ------------------------------------------------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// shared::cluster address of the same shared variable in CTA `rank` of this cluster
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-// all threads of all CTAs of the cluster
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// arrive on an mbarrier of any CTA of the cluster (shared::cluster address)
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(ex_smem_u32(smem_result)),
-               "r"(ncols)
-               : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-// D[tmem of both CTAs] (+)= A[smem of both CTAs] * B[smem of both CTAs]^T, int8 -> int32; issued by the even CTA
-__device__ __forceinline__ void tc_mma_i8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                               uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Arrive once on the mbarrier at this shared offset in both CTAs of the pair when the pair MMAs issued so far by
-// this thread have completed (an MMA-completion signal; it moves no data).
-__device__ __forceinline__ void tc_commit_pair_both(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          ex_smem_u32(bar)),
-      "h"((uint16_t)3)
-      : "memory");
-}
-// Same, on this CTA's mbarrier only.
-__device__ __forceinline__ void tc_commit_pair_self(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(ex_smem_u32(bar))
-               : "memory");
-}
-// 2D tiled TMA load into this CTA's shared memory whose completion (transaction bytes) is counted on the mbarrier at
-// `bar_cluster` (the even CTA's barrier of the pair). A plain load: no multicast.
-__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t bar_cluster, int c0,
-                                                 int c1, uint64_t cache_hint) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
-      "[%1, {%3, %4}], [%2], %5;" ::"r"(ex_smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(c0), "r"(c1), "l"(cache_hint)
-      : "memory");
-}
 
 // Shared-memory matrix descriptor for a K-major operand tile in the 128-byte swizzled layout written by TMA
 // (CU_TENSOR_MAP_SWIZZLE_128B): rows of 128 bytes, 8-row atoms of 1024 bytes. Fields (sm_100 UMMA descriptor):
@@ -316,14 +234,10 @@ __device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr) {
   return d;
 }
 
-// Instruction descriptor of tcgen05.mma (sm_100): D format in bits [4,6) (1 = f32, 2 = s32), A format [7,10),
-// B format [10,13) (kind::f16: 1 = bf16; kind::i8: 1 = signed), A/B K-major (bits 15,16 = 0), N >> 3 in [17,23),
-// M >> 4 in [24,29).
+// Instruction descriptor of tcgen05.mma kind::i8 (sm_100): D format in bits [4,6) (2 = s32), A and B formats in
+// [7,10) and [10,13) (1 = signed int8), A/B K-major (bits 15,16 = 0), N >> 3 in [17,23), M >> 4 in [24,29).
 __host__ __device__ constexpr uint32_t make_idesc_i8(int M, int N) {
   return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-__host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 __device__ __forceinline__ uint32_t elect_one() {
@@ -353,27 +267,6 @@ static cudaError_t ex_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-}
-
-// Same, launched as clusters of `cluster_x` CTAs along x (1: an ordinary launch).
-template <typename... KArgs, typename... Args>
-static cudaError_t ex_launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                                         cudaStream_t st, int cluster_x, Args&&... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = (unsigned)cluster_x;
-  attr[1].val.clusterDim.y = 1;
-  attr[1].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = cluster_x > 1 ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 

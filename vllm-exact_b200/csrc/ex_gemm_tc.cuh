@@ -86,30 +86,23 @@ __device__ __forceinline__ void tmem_ldc(uint32_t taddr, uint32_t (&r)[CW]) {
     tmem_ld8(taddr, r);
 }
 
-template <int BT, bool PAIR = false>
+template <int BT>
 struct TcLayout {
-  static constexpr int XROWS = PAIR ? BT / 2 : BT;  // tokens of the activation tile held by this CTA
-  static constexpr int XH = XROWS * TC_BK;           // bytes of its xh rows (its xl rows follow)
-  static constexpr int XTILE = 2 * XH;               // bytes of the stacked activation tile
+  static constexpr int XH = BT * TC_BK;    // bytes of the tile's xh rows (its xl rows follow)
+  static constexpr int XTILE = 2 * XH;     // bytes of the stacked activation tile
   static constexpr int STAGE = 2 * TC_WTILE + XTILE;
-  static constexpr int WROWS = PAIR ? 256 : 128;     // weight rows of one n-tile
-  static constexpr int CB_TRUNC = 2 * BT;       // TMEM columns per accumulator buffer
+  static constexpr int WROWS = 128;        // weight rows of one n-tile
+  static constexpr int CB_TRUNC = 2 * BT;  // TMEM columns per accumulator buffer
   static constexpr int CB_FULL = 3 * BT;
   static_assert(BT % 8 == 0 && BT >= 8 && BT <= 128, "token tile");
 };
 
-// PAIR: the kernel runs as clusters of two CTAs and every MMA is a cta_group::2 MMA of M = 256 issued by the even
-// CTA: each CTA loads its own 128 weight rows and one half of the tile's tokens (same shared-memory offsets in both),
-// the loads of both CTAs complete on the even CTA's full barrier, the even CTA's commits release the stages and
-// publish the accumulators of both CTAs, and each CTA's epilogue finishes its own 128 rows. Per CTA and K step that
-// is 48 KB of operands for the MMA work that costs 64 KB single-CTA.
-template <int BT, bool PAIR>
+template <int BT>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     k_exact_tc_i8(const __grid_constant__ CUtensorMap tm_wh, const __grid_constant__ CUtensorMap tm_wl,
                   const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl,
                   const TcArgs a) {
-  static_assert(!PAIR || BT == 128, "CTA pairs use the 128-token tile");
-  using Lay = TcLayout<BT, PAIR>;
+  using Lay = TcLayout<BT>;
   extern __shared__ uint8_t tc_smem_raw[];
   // 1024-byte alignment for the 128-byte-swizzled tiles
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -139,7 +132,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(tfull_bar + i, 1);
-      mbar_init(tempty_bar + i, (PAIR ? 2 : 1) * 32 * TC_EPI_WARPS);  // pairs: both CTAs' epilogues
+      mbar_init(tempty_bar + i, 32 * TC_EPI_WARPS);
     }
     mbar_init(done_bar, 1);
     mbar_init(epi_bar, 32 * TC_EPI_WARPS);
@@ -153,22 +146,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tma_prefetch_desc(&tm_xl);
   }
   if (warp == 1) {
-    if constexpr (PAIR) {
-      tmem_alloc_pair(tmem_slot, TC_TMEM_COLS);  // the same columns in both CTAs of the pair
-      tmem_relinquish_pair();
-    } else {
-      tmem_alloc(tmem_slot, TC_TMEM_COLS);
-      tmem_relinquish();
-    }
+    tmem_alloc(tmem_slot, TC_TMEM_COLS);
+    tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
-  if constexpr (PAIR) cluster_sync_all();  // the peer's barriers and TMEM exist before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;  // 0: the pair's MMA issuer
-  const int wrow_off = (int)rank * 128;                  // this CTA's first weight row inside an n-tile
-  const int xrow_off = (int)rank * Lay::XROWS;           // this CTA's first token inside an m-tile
 
   // Programmatic dependent launch: this prologue may overlap the previous kernel (typically the activation
   // digitizer). Before waiting, only warm L2 with this CTA's first weight tiles (L2 is coherent with any writer, so
@@ -181,8 +165,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     while (left > 0 && walk.next(sg)) {
       const int n_tile = sg.n_tile;
       for (int kt = sg.kb; kt < sg.ke && left > 0; ++kt, --left) {
-        tma_prefetch_l2_2d(&tm_wh, kt * TC_BK, n_tile * Lay::WROWS + wrow_off);
-        tma_prefetch_l2_2d(&tm_wl, kt * TC_BK, n_tile * Lay::WROWS + wrow_off);
+        tma_prefetch_l2_2d(&tm_wh, kt * TC_BK, n_tile * Lay::WROWS);
+        tma_prefetch_l2_2d(&tm_wl, kt * TC_BK, n_tile * Lay::WROWS);
       }
     }
   }
@@ -209,22 +193,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
           uint8_t* st = smem + (size_t)stage * Lay::STAGE;
           const int kc = kt * TC_BK;
-          const int wr = n_tile * Lay::WROWS + wrow_off, xr = m_tile * BT + xrow_off;
-          if constexpr (PAIR) {
-            // both CTAs' bytes complete on the even CTA's full barrier, which only the even CTA arms
-            if (rank == 0) mbar_arrive_expect_tx(full_bar + stage, 2 * Lay::STAGE);
-            const uint32_t fb = mapa_shared(ex_smem_u32(full_bar + stage), 0);
-            tma_load_2d_pair(st, &tm_wh, fb, kc, wr, pol_w);
-            tma_load_2d_pair(st + TC_WTILE, &tm_wl, fb, kc, wr, pol_w);
-            tma_load_2d_pair(st + 2 * TC_WTILE, &tm_xh, fb, kc, xr, pol_x);
-            tma_load_2d_pair(st + 2 * TC_WTILE + Lay::XH, &tm_xl, fb, kc, xr, pol_x);
-          } else {
-            mbar_arrive_expect_tx(full_bar + stage, Lay::STAGE);
-            tma_load_2d(st, &tm_wh, full_bar + stage, kc, wr, pol_w);
-            tma_load_2d(st + TC_WTILE, &tm_wl, full_bar + stage, kc, wr, pol_w);
-            tma_load_2d(st + 2 * TC_WTILE, &tm_xh, full_bar + stage, kc, xr, pol_x);
-            tma_load_2d(st + 2 * TC_WTILE + Lay::XH, &tm_xl, full_bar + stage, kc, xr, pol_x);
-          }
+          const int wr = n_tile * Lay::WROWS, xr = m_tile * BT;
+          mbar_arrive_expect_tx(full_bar + stage, Lay::STAGE);
+          tma_load_2d(st, &tm_wh, full_bar + stage, kc, wr, pol_w);
+          tma_load_2d(st + TC_WTILE, &tm_wl, full_bar + stage, kc, wr, pol_w);
+          tma_load_2d(st + 2 * TC_WTILE, &tm_xh, full_bar + stage, kc, xr, pol_x);
+          tma_load_2d(st + 2 * TC_WTILE + Lay::XH, &tm_xl, full_bar + stage, kc, xr, pol_x);
           ++issued;
           if (++stage == S) {
             stage = 0;
@@ -232,27 +206,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
         }
       }
-      // wait for every load still in flight before the CTA may exit (bounded); the odd CTA of a pair sees its loads
-      // land through the release of the stage (the MMA that read them has completed)
+      // wait for every load still in flight before the CTA may exit (bounded)
       const int64_t pending = issued < S ? issued : S;
       for (int64_t i = 0; i < pending; ++i) {
         if (--stage < 0) {
           stage = S - 1;
           phase ^= 1;
         }
-        if (PAIR && rank != 0)
-          mbar_wait(empty_bar + stage, phase, EX_DEVERR_WAIT_TMA);
-        else
-          mbar_wait(full_bar + stage, phase, EX_DEVERR_WAIT_TMA);
+        mbar_wait(full_bar + stage, phase, EX_DEVERR_WAIT_TMA);
       }
     }
     __syncwarp();  // reconverge the warp before the CTA barrier below (lane 0 alone ran the producer)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0 && rank == 0) {
+    if (lane == 0) {
       const uint32_t idesc_2bt = make_idesc_i8(128, 2 * BT);
       const uint32_t idesc_bt = make_idesc_i8(128, BT);
-      const uint32_t idesc_pair = make_idesc_i8(256, BT);
       TcWalk walk(a, (int)blockIdx.x);
       TcSeg sg;
       int stage = 0;
@@ -282,40 +251,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           for (int j = 0; j < TC_BK / 32; ++j) {  // 32-byte K steps inside the swizzled row (+2 in 16-byte units)
             const uint64_t o = (uint64_t)(2 * j);
             const uint32_t acc = (kt > sg.kb || j > 0) ? 1u : 0u;
-            if constexpr (PAIR) {
-              // xh and xl are separate B operands here (each CTA holds half of each), so md takes two MMAs
-              tc_mma_i8_pair(d_hh, dwh + o, dxh + o, idesc_pair, acc);
-              tc_mma_i8_pair(d_md, dwh + o, dxl + o, idesc_pair, acc);
-              tc_mma_i8_pair(d_md, dwl + o, dxh + o, idesc_pair, 1u);
-              if (!a.trunc) tc_mma_i8_pair(d_ll, dwl + o, dxl + o, idesc_pair, acc);
-            } else {
-              tc_mma_i8(d_hh, dwh + o, dxh + o, idesc_2bt, acc);
-              tc_mma_i8(d_md, dwl + o, dxh + o, idesc_bt, 1u);
-              if (!a.trunc) tc_mma_i8(d_ll, dwl + o, dxl + o, idesc_bt, acc);
-            }
+            tc_mma_i8(d_hh, dwh + o, dxh + o, idesc_2bt, acc);
+            tc_mma_i8(d_md, dwl + o, dxh + o, idesc_bt, 1u);
+            if (!a.trunc) tc_mma_i8(d_ll, dwl + o, dxl + o, idesc_bt, acc);
           }
-          // frees this smem stage (in both CTAs of a pair) once the MMAs above have read it
-          if constexpr (PAIR)
-            tc_commit_pair_both(empty_bar + stage);
-          else
-            tc_commit(empty_bar + stage);
+          // frees this smem stage once the MMAs above have read it
+          tc_commit(empty_bar + stage);
           if (++stage == S) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        // accumulator of this segment is complete (in both CTAs of a pair)
-        if constexpr (PAIR)
-          tc_commit_pair_both(tfull_bar + buf);
-        else
-          tc_commit(tfull_bar + buf);
+        // accumulator of this segment is complete
+        tc_commit(tfull_bar + buf);
         ++seg_i;
       }
-      if constexpr (PAIR)
-        tc_commit_pair_self(done_bar);
-      else
-        tc_commit(done_bar);
+      tc_commit(done_bar);
       mbar_wait(done_bar, 0, EX_DEVERR_WAIT_MMA);
     }
     __syncwarp();  // reconverge the warp before the CTA barrier below (lane 0 alone issued the MMAs)
@@ -341,7 +293,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int buf = nbuf == 2 ? (seg_i & 1) : 0;
       const uint32_t use = nbuf == 2 ? (uint32_t)(seg_i >> 1) : (uint32_t)seg_i;
       const int n_tile = sg.n_tile, m_tile = sg.m_tile;
-      const int n = n_tile * Lay::WROWS + wrow_off + row;
+      const int n = n_tile * Lay::WROWS + row;
       const int m0 = m_tile * BT;
       // scale words of this tile, fetched while the MMAs still run (global latency is long under full HBM load)
       __syncwarp();  // the previous segment's reads of my_sx / my_cx are done
@@ -359,18 +311,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       // Slot layout: [lane quarter][token][32 rows].
       // A split tile (m, n) owns slot (b* - 1) * m_tiles + m, b* = the first group boundary strictly inside n's
       // k-range: every contributor computes the same slot and distinct split tiles get distinct slots.
-      int slot = whole ? 0 : tc_split_slot(a, n_tile, m_tile);
-      if (PAIR) slot = 2 * slot + (int)rank;  // each CTA of a pair owns the half of the slot holding its rows
+      const int slot = whole ? 0 : tc_split_slot(a, n_tile, m_tile);
       long long* slot_q = a.ws_acc + ((int64_t)slot * 4 + q) * BT * 32;
-      // the pair's TMEM-empty barrier lives in the even CTA (the MMA issuer)
-      const uint32_t tempty_addr = PAIR ? mapa_shared(ex_smem_u32(tempty_bar + buf), 0) : 0u;
       const uint32_t t_hh = tmem_base + lane_off + (uint32_t)(buf * cb);
       if (half >= NCH) {  // no chunk for this warp (BT = 8): release the accumulator right away
         tc_fence_before();
-        if constexpr (PAIR)
-          mbar_arrive_cluster(tempty_addr);
-        else
-          mbar_arrive(tempty_bar + buf);
+        mbar_arrive(tempty_bar + buf);
       }
 #pragma unroll 1
       for (int ci = half; ci < NCH; ci += 2) {
@@ -382,10 +328,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tmem_ld_wait();
         if (ci + 2 >= NCH) {  // this warp's TMEM reads of the buffer are done: hand it back to the MMA warp
           tc_fence_before();
-          if constexpr (PAIR)
-            mbar_arrive_cluster(tempty_addr);
-          else
-            mbar_arrive(tempty_bar + buf);
+          mbar_arrive(tempty_bar + buf);
         }
         if (whole) {
           long long tot[CW];
@@ -464,13 +407,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
-  if constexpr (PAIR) cluster_sync_all();  // neither CTA frees TMEM or exits while its peer may still signal it
   if (warp == 1) {
     tc_fence_after();
-    if constexpr (PAIR)
-      tmem_dealloc_pair(tmem_base, TC_TMEM_COLS);
-    else
-      tmem_dealloc(tmem_base, TC_TMEM_COLS);
+    tmem_dealloc(tmem_base, TC_TMEM_COLS);
   }
 }
 
@@ -534,14 +473,12 @@ static bool encode_2d_i8(CUtensorMap* map, const void* base, uint64_t inner, uin
   return r == CUDA_SUCCESS;
 }
 
-template <int BT, bool PAIR = false>
+template <int BT>
 static cudaError_t launch_tc_bt(const TcPlan& p, const TcArgs& a, const CUtensorMap& mwh, const CUtensorMap& mwl,
                                 const CUtensorMap& mxh, const CUtensorMap& mxl, cudaStream_t st) {
-  cudaError_t e =
-      cudaFuncSetAttribute(k_exact_tc_i8<BT, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
+  cudaError_t e = cudaFuncSetAttribute(k_exact_tc_i8<BT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
   if (e != cudaSuccess) return e;
-  return ex_launch_pdl_cluster(k_exact_tc_i8<BT, PAIR>, dim3(p.G), dim3(TC_THREADS), p.smem, st, PAIR ? 2 : 1, mwh,
-                               mwl, mxh, mxl, a);
+  return ex_launch_pdl(k_exact_tc_i8<BT>, dim3(p.G), dim3(TC_THREADS), p.smem, st, mwh, mwl, mxh, mxl, a);
 }
 
 template <bool PARTIAL>
@@ -551,8 +488,7 @@ static cudaError_t launch_tc(const TcPlan& p, int F, int trunc, int out_dtype, c
                              int64_t ldo, void* ws, cudaStream_t st) {
   CUtensorMap mwh, mwl, mxh, mxl;
   if (!encode_2d_i8(&mwh, wh, K, N, ldw, TC_BK, 128) || !encode_2d_i8(&mwl, wl, K, N, ldw, TC_BK, 128) ||
-      !encode_2d_i8(&mxh, xh, K, M, ldx, TC_BK, p.pair ? p.BT / 2 : p.BT) ||
-      !encode_2d_i8(&mxl, xl, K, M, ldx, TC_BK, p.pair ? p.BT / 2 : p.BT))
+      !encode_2d_i8(&mxh, xh, K, M, ldx, TC_BK, p.BT) || !encode_2d_i8(&mxl, xl, K, M, ldx, TC_BK, p.BT))
     return cudaErrorNotSupported;
   TcArgs a;
   a.cx = cx;
@@ -571,7 +507,6 @@ static cudaError_t launch_tc(const TcPlan& p, int F, int trunc, int out_dtype, c
   a.out_dtype = out_dtype;
   a.partial = PARTIAL ? 1 : 0;
   tc_plan_args(p, a);
-  if (p.pair) return launch_tc_bt<128, true>(p, a, mwh, mwl, mxh, mxl, st);
   switch (p.BT) {
     case 8: return launch_tc_bt<8>(p, a, mwh, mwl, mxh, mxl, st);
     case 16: return launch_tc_bt<16>(p, a, mwh, mwl, mxh, mxl, st);

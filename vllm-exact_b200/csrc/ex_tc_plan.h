@@ -38,8 +38,7 @@ struct TcPlan {
   int gs;        // CTAs per group (one per m-tile of a chunk)
   int groups;    // groups; group g walks (n-tile, k) range [T*g/groups, T*(g+1)/groups)
   int chunks;    // passes over the range: m-tiles c*gs + j for c < chunks
-  int G;         // CTAs = groups * gs (* 2 for CTA pairs)
-  int pair;      // 1: CTA pairs (tcgen05 cta_group::2), n-tiles of 256 weight rows; BT = 128
+  int G;         // CTAs = groups * gs
   int stages;
   size_t smem;
   size_t ws_bytes;
@@ -61,7 +60,6 @@ struct TcArgs {
   int64_t T;  // n_tiles * KI
   int gs, groups, chunks;
   int stages;
-  int pair;  // 0 or 1: CTAs blockIdx.x and blockIdx.x ^ 1 form a pair that shares every tile
 };
 
 struct TcSeg {
@@ -72,14 +70,13 @@ struct TcSeg {
 // k-iteration) range [T*g/groups, T*(g+1)/groups) once for each m-tile chunk c, on m-tile c*gs + j. Siblings run in
 // lockstep over the same weight k-slices, so a weight tile leaves HBM once per chunk and the other siblings read it
 // from L2 (one m-tile: the original one-range-per-CTA partition). 32-bit arithmetic whenever the products fit.
-// `cta` is the CTA's index in the grid (blockIdx.x); both CTAs of a pair walk the same segments.
+// `cta` is the CTA's index in the grid (blockIdx.x).
 struct TcWalk {
   int64_t r0, r1, it;
   int KI, j, mc, chunks, gs, m_tiles;
   EX_HD TcWalk(const TcArgs& a, int cta) {
-    const int u = cta >> a.pair;
-    const int g = u / a.gs;
-    j = u % a.gs;
+    const int g = cta / a.gs;
+    j = cta % a.gs;
     if (a.T * (int64_t)a.groups < 2147483647ll) {
       const uint32_t T = (uint32_t)a.T, G = (uint32_t)a.groups, b = (uint32_t)g;
       r0 = (int64_t)((T * b) / G);
@@ -123,7 +120,7 @@ struct TcWalk {
 
 // Workspace slot of a split tile (a segment with kb > 0 or ke < KI): slot (b* - 1) * m_tiles + m_tile, b* = the first
 // group boundary strictly inside n_tile's k-range. Every contributor of the tile computes the same slot and distinct
-// split tiles get distinct slots in [0, (groups - 1) * m_tiles). CTA pairs use slot 2 * s + rank (one half each).
+// split tiles get distinct slots in [0, (groups - 1) * m_tiles).
 EX_HD int tc_split_slot(const TcArgs& a, int n_tile, int m_tile) {
   const int64_t num = ((int64_t)n_tile * a.KI + 1) * a.groups + a.T - 1;
   const int bstar = num < 2147483647ll ? (int)((uint32_t)num / (uint32_t)a.T) : (int)(num / a.T);
@@ -138,25 +135,19 @@ inline int tc_pick_bt(int64_t M) {
   return 128;
 }
 
-inline size_t tc_stage_bytes(int BT, bool pair) {
-  return 2 * (size_t)TC_WTILE + 2 * (size_t)(pair ? BT / 2 : BT) * TC_BK;
-}
+inline size_t tc_stage_bytes(int BT) { return 2 * (size_t)TC_WTILE + 2 * (size_t)BT * TC_BK; }
 
-// EX_ALGO_TC_I8_PAIR plans CTA pairs on 256-row n-tiles and 128-token m-tiles; every other algorithm value plans
-// single CTAs with the token tile picked from M.
-inline TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int split_k, int algo, int sms) {
+// Single CTAs on 128-row n-tiles with the token tile picked from M.
+inline TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int split_k, int sms) {
   TcPlan p;
-  const bool pair = (algo == EX_ALGO_TC_I8_PAIR);
-  p.pair = pair ? 1 : 0;
-  p.BT = pair ? 128 : tc_pick_bt(M);
+  p.BT = tc_pick_bt(M);
   p.m_tiles = (int)((M + p.BT - 1) / p.BT);
-  p.n_tiles = pair ? (int)((N + 255) / 256) : (int)((N + 127) / 128);
+  p.n_tiles = (int)((N + 127) / 128);
   p.KI = (int)((K + TC_BK - 1) / TC_BK);
   p.T = (int64_t)p.n_tiles * p.KI;
   p.gs = std::min(p.m_tiles, 8);
   p.chunks = (p.m_tiles + p.gs - 1) / p.gs;
-  const int units = pair ? sms / 2 : sms;  // CTA pairs or CTAs resident at once (one per SM)
-  const int64_t fit = std::max<int64_t>(1, units / p.gs);  // groups resident at once
+  const int64_t fit = std::max<int64_t>(1, sms / p.gs);  // groups resident at once (one CTA per SM)
   int64_t groups = fit;  // automatic default: the balanced (n-tile, k-step) partition over every resident group
   if (split_k > 0) {
     groups = (int64_t)p.n_tiles * split_k;
@@ -171,16 +162,15 @@ inline TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int split_k, int algo, in
   groups = std::max<int64_t>(1, std::min<int64_t>(groups, p.T));
   groups = std::min<int64_t>(groups, 2147483647 / p.gs);
   p.groups = (int)groups;
-  p.G = p.groups * p.gs * (pair ? 2 : 1);
-  const size_t stage = tc_stage_bytes(p.BT, pair);
+  p.G = p.groups * p.gs;
+  const size_t stage = tc_stage_bytes(p.BT);
   const size_t overhead = 1024 + 256 + TC_RED_STAGING + TC_TOK_WORDS;  // alignment, barriers, staging, scale words
   p.stages = (int)std::min<size_t>(8, (TC_SMEM_BUDGET - overhead) / stage);
   p.smem = (size_t)p.stages * stage + overhead;
   const bool aligned = (groups <= p.n_tiles) && (p.n_tiles % groups == 0);  // every group covers whole n-tiles
   const int64_t slots = (groups - 1) * (int64_t)p.m_tiles;  // one per (group boundary, m-tile)
-  const int halves = pair ? 2 : 1;                           // a pair's slot has one half per CTA (128 rows each)
-  p.cnt_bytes = (size_t)((slots * halves * 4 + 255) / 256 * 256);
-  p.ws_bytes = (aligned || slots == 0) ? 0 : p.cnt_bytes + (size_t)slots * halves * p.BT * 128 * 8;
+  p.cnt_bytes = (size_t)((slots * 4 + 255) / 256 * 256);
+  p.ws_bytes = (aligned || slots == 0) ? 0 : p.cnt_bytes + (size_t)slots * p.BT * 128 * 8;
   // (slot layout [4 lane quarters][BT tokens][32 rows] per 128 rows: each epilogue warp reduces contiguous 1 KB)
   return p;
 }
@@ -195,7 +185,6 @@ inline void tc_plan_args(const TcPlan& p, TcArgs& a) {
   a.groups = p.groups;
   a.chunks = p.chunks;
   a.stages = p.stages;
-  a.pair = p.pair;
 }
 
 }  // namespace ex

@@ -12,7 +12,7 @@ LIB_PATH = Path(os.environ.get("VLLM_EXACT_B200_LIB", Path(__file__).with_name("
 EX_OK, EX_ERR_ARG, EX_ERR_ALIGN, EX_ERR_WORKSPACE, EX_ERR_DTYPE, EX_ERR_UNSUPPORTED, EX_ERR_CUDA, EX_ERR_DEVICE = range(8)
 EX_DTYPE_F32, EX_DTYPE_BF16, EX_DTYPE_F16 = 0, 1, 2
 EX_IPC_HANDLE_BYTES = 64
-EX_ALGO_AUTO, EX_ALGO_SIMT, EX_ALGO_TC_I8, EX_ALGO_TC_BF16, EX_ALGO_TC_I8_PAIR = 0, 1, 2, 3, 4
+EX_ALGO_AUTO, EX_ALGO_SIMT, EX_ALGO_TC_I8 = 0, 1, 2
 
 c_i64, c_i32, c_vp, c_sz, c_f32 = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_float
 
@@ -31,6 +31,8 @@ SIGNATURES = {
                           c_i32, c_vp, c_i32, c_i64, c_vp, c_sz, c_i32, c_i32, c_vp]),
     "ex_linear_noalloc": (c_i32, [c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64,
                                   c_i32, c_i32, c_vp, c_i32, c_i64, c_i32, c_i32, c_vp]),
+    "ex_linear_noalloc_reset": (c_i32, [c_vp]),
+    "ex_linear_noalloc_fill_scratch": (c_i32, [c_i32, c_vp]),
     "ex_linear_partial_i64": (c_i32, [c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i32,
                                       c_i32, c_vp, c_i64, c_vp, c_sz, c_i32, c_i32, c_vp]),
     "ex_epilogue_i64": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_vp, c_i32, c_i64, c_vp]),
@@ -49,6 +51,7 @@ SIGNATURES = {
 }
 
 _LIB = None
+ON_DEVICE_ERROR = []  # callables run when device_error() reports an error (e.g. re-zeroing split-K workspaces)
 
 
 class ExactError(RuntimeError):
@@ -85,7 +88,12 @@ def check(fn_name, status):
 
 
 def device_error() -> int:
-    """Synchronize, return and clear the device error word (0 = no bounded wait timed out)."""
+    """Synchronize, return and clear the device error word (0 = no bounded wait timed out). On an error, the
+    library re-zeroes the static scratch of ex_linear_noalloc and the hooks in ON_DEVICE_ERROR re-zero the split-K
+    workspaces this package owns, since a call stopped by a timed-out wait may have left partial sums in them."""
     code = c_i32(0)
     check("ex_device_error", lib().ex_device_error(ctypes.byref(code)))
+    if code.value != 0:
+        for fn in ON_DEVICE_ERROR:
+            fn()
     return code.value

@@ -22,11 +22,11 @@ import threading
 import torch
 
 from . import _lib
-from ._lib import EX_ALGO_AUTO, EX_ALGO_SIMT, EX_ALGO_TC_BF16, EX_ALGO_TC_I8, EX_ALGO_TC_I8_PAIR, check, lib
+from ._lib import EX_ALGO_AUTO, EX_ALGO_SIMT, EX_ALGO_TC_I8, check, lib
 
 __all__ = ["digitize", "digitize_weight", "exact_linear", "exact_linear_partial_i64", "exact_epilogue",
-           "autotune_exact", "EXACT_CFGS", "reserve_workspace", "EX_ALGO_AUTO", "EX_ALGO_SIMT", "EX_ALGO_TC_I8",
-           "EX_ALGO_TC_BF16", "EX_ALGO_TC_I8_PAIR"]
+           "autotune_exact", "EXACT_CFGS", "reserve_workspace", "reset_workspaces", "EX_ALGO_AUTO", "EX_ALGO_SIMT",
+           "EX_ALGO_TC_I8"]
 
 _DT = {torch.float32: _lib.EX_DTYPE_F32, torch.bfloat16: _lib.EX_DTYPE_BF16, torch.float16: _lib.EX_DTYPE_F16}
 _LD_ALIGN = 16  # digit rows are padded to 16 bytes so the tensor-core kernels can TMA them
@@ -46,10 +46,16 @@ def _need_cuda(*ts):
 # split-K workspace: zero-filled once, every call returns it to zero
 # ------------------------------------------------------------------------------------------------------------------
 _WS = {}
+_WS_RETIRED = []  # outgrown workspaces, kept alive: CUDA graphs captured earlier may still use them
 _WS_LOCK = threading.Lock()
 
 
 def _workspace(dev: torch.device, nbytes: int, stream: int | None = None) -> torch.Tensor | None:
+    """The split-K workspace of (device, stream), grown geometrically. A workspace is never freed once it has been
+    handed out: a CUDA graph captured with it keeps its address, so a later, larger call (for instance vLLM capturing
+    a bigger batch after a smaller one) gets a new workspace and the old one stays valid for the old graph. A
+    workspace first allocated during a capture is zero-filled by that graph's replays (the fill is captured too), and
+    every call leaves it zero again."""
     if nbytes <= 0:
         return None
     key = (dev.index, _stream(dev) if stream is None else stream)
@@ -57,9 +63,22 @@ def _workspace(dev: torch.device, nbytes: int, stream: int | None = None) -> tor
         ws = _WS.get(key)
         if ws is None or ws.numel() < nbytes:
             size = max(nbytes, 2 * (ws.numel() if ws is not None else 0), 1 << 20)
+            if ws is not None:
+                _WS_RETIRED.append(ws)
             ws = torch.zeros(size, dtype=torch.uint8, device=dev)
             _WS[key] = ws
     return ws
+
+
+def reset_workspaces() -> None:
+    """Re-zero every split-K workspace (current and retired). Needed only after a device error: a call stopped by a
+    timed-out wait can leave partial sums behind (_lib.device_error() runs this when it reports an error)."""
+    with _WS_LOCK:
+        for ws in list(_WS.values()) + _WS_RETIRED:
+            ws.zero_()
+
+
+_lib.ON_DEVICE_ERROR.append(reset_workspaces)
 
 
 def reserve_workspace(nbytes: int, device=None, stream=None) -> None:
@@ -120,16 +139,16 @@ def digitize_weight(w: torch.Tensor, F: int, rows_per_block: int = 32768):
 # ------------------------------------------------------------------------------------------------------------------
 def _parse_cfg(cfg):
     """cfg: None (automatic), {"algo": ..., "split_k": ...}, or a reference-style tuple
-    (BM, BN, BK, warps, stages, GM[, split_k[, mma]]) where only split_k and mma (0 = INT8 tensor cores, 1 = bf16
-    tensor cores) carry meaning here; the Triton tile sizes have no counterpart."""
+    (BM, BN, BK, warps, stages, GM[, split_k[, mma]]) where only split_k carries meaning here. The reference's mma
+    flag (0 = INT8, 1 = bf16 tensor cores, same bits either way) selects the INT8 tensor-core kernel for both values:
+    B200 runs INT8 MMAs at twice the bf16 rate, so a bf16-digit kernel could only be slower. The Triton tile sizes
+    have no counterpart."""
     if cfg is None:
         return EX_ALGO_AUTO, 0
     if isinstance(cfg, dict):
         return int(cfg.get("algo", EX_ALGO_AUTO)), int(cfg.get("split_k", 0))
     sk = int(cfg[6]) if len(cfg) > 6 else 0
-    algo = EX_ALGO_AUTO
-    if len(cfg) > 7:
-        algo = EX_ALGO_TC_BF16 if cfg[7] == 1 else EX_ALGO_TC_I8
+    algo = EX_ALGO_TC_I8 if len(cfg) > 7 else EX_ALGO_AUTO
     return algo, sk
 
 
@@ -154,7 +173,6 @@ def _operands(xd, wd):
 # (kernels.py:250-253); the B200 kernels choose their tiles from the shape, so a configuration selects what is left
 # free: the algorithm and the split-K factor (0 = the automatic plan of that algorithm). Every one gives the same bits.
 EXACT_CFGS = ([{"algo": EX_ALGO_TC_I8, "split_k": s} for s in (0, 1, 2, 4, 8)] +
-              [{"algo": EX_ALGO_TC_I8_PAIR, "split_k": s} for s in (0, 1, 2)] +
               [{"algo": EX_ALGO_SIMT, "split_k": 0}])
 _CFG_CACHE = {}  # (M, N, K, F, trunc) -> configuration chosen by autotune_exact
 
