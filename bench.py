@@ -184,7 +184,8 @@ def make_activation(M, K, seed, dev):
 
 
 def make_weight_digits(K, N, seed, dev, F=14):
-    """Weights ~N(0, 0.02) in bf16, digitized at load time like the plugin (kernels.digitize_weight)."""
+    """Weights ~N(0, 0.02) in bf16, digitized at load time like the plugin (kernels.digitize_weight: generated and
+    digitized in row blocks to bound memory, then marked static as digitize_weight marks its result)."""
     import torch
     from vllm_exact import kernels as KK
     g = torch.Generator(device=dev).manual_seed(seed)
@@ -193,6 +194,7 @@ def make_weight_digits(K, N, seed, dev, F=14):
         j = min(N, i + 16384)
         w = (torch.randn(j - i, K, generator=g, device=dev) * 0.02).bfloat16()
         KK.digitize(w, F, out=tuple(t[i:j] for t in out))
+    KK.mark_static(*out)
     return out
 
 
@@ -226,39 +228,43 @@ def run_ours(args):
     KK.reserve_workspace(max(KK.lib().ex_linear_workspace_bytes(M, N, K, 0, 0) for M, _, K, N in order), dev,
                          stream=stream)
 
-    def one_step(ev=None):
-        n = 0
-        for i, (M, name, K, N) in enumerate(order):
-            xd = KK.digitize(X[(M, name)], 14)
-            if ev is not None:
-                ev[i][0].record()
-            KK.exact_linear(xd, W[name], 14, True, out=Y[(M, name)])
-            if ev is not None:
-                ev[i][1].record()
-            n += 2
-        return n
+    def one_step():
+        for M, name, K, N in order:
+            KK.exact_linear(KK.digitize(X[(M, name)], 14), W[name], 14, True, out=Y[(M, name)])
+        return 2 * len(order)
 
-    # CUDA graphs, as vLLM runs decode: graph A = one step; graphs B_r = one step with timing events around each GEMM
-    R = min(10, args.steps)
+    # the same 15 GEMMs on digits computed once: the GEMM kernel alone, back to back (roofline timing basis)
+    XD = {key: KK.digitize(x, 14) for key, x in X.items()}
+
+    def gemm_step():
+        for M, name, K, N in order:
+            KK.exact_linear(XD[(M, name)], W[name], 14, True, out=Y[(M, name)])
+
+    # CUDA graphs, as vLLM runs decode: graph A = one step; graph G = the step's GEMMs alone. No timing events inside
+    # either graph: events between launches break the programmatic-dependent-launch overlap and add microseconds.
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             one_step()
+            gemm_step()
     torch.cuda.synchronize()
     gA = torch.cuda.CUDAGraph()
     with torch.cuda.graph(gA, stream=stream):
         launches_per_step = one_step()
-    evB = [[[torch.cuda.Event(enable_timing=True, external=True) for _ in range(2)] for _ in order] for _ in range(R)]
-    gB = []
-    for r in range(R):
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            one_step(evB[r])
-        gB.append(g)
+    gG = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gG, stream=stream):
+        gemm_step()
     for _ in range(args.warmup):
+        gG.replay()
         gA.replay()
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t2, t3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t2.record()
+        for _ in range(args.steps):
+            gG.replay()
+        t3.record()
+    torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         clk.wait_first_sample()
         if world > 1:
@@ -272,14 +278,6 @@ def run_ours(args):
             t1.record()
         torch.cuda.synchronize()
         c1 = clk.mark()
-        with torch.cuda.stream(stream):
-            # per-GEMM durations from the last R steps of a second timed pass
-            t2.record()
-            for _ in range(max(args.steps // R, 1)):
-                for g in gB:
-                    g.replay()
-            t3.record()
-        torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     ms = t0.elapsed_time(t1)
@@ -287,17 +285,12 @@ def run_ours(args):
         tt = torch.tensor([ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt)
-    ms_events = t2.elapsed_time(t3) / (max(args.steps // R, 1) * R)
-    gemm_ms = sum(a.elapsed_time(b) for step in evB for a, b in step)
-    per_gemm = {}
-    for i, (M, name, K, N) in enumerate(order):
-        us = 1000 * statistics.median(evB[r][i][0].elapsed_time(evB[r][i][1]) for r in range(R))
-        per_gemm[f"{name}/M{M}"] = {"us": round(us, 2), "GBps": round(gemm_bytes(M, K, N) / us / 1e3, 1),
-                                    "frac_hbm": round(gemm_bytes(M, K, N) / us / 1e3 / hbm, 3)}
+    gemm_ms = t2.elapsed_time(t3) / args.steps
     ms_per_step = ms / args.steps
     value = world * step_bytes / (ms_per_step * 1e-3) / 1e12
-    achieved = R * step_bytes / (gemm_ms * 1e-3) / 1e9  # GB/s over the GEMM launches only
+    achieved = step_bytes / (gemm_ms * 1e-3) / 1e9  # GB/s of the GEMM launches alone
     launches = {"n": launches_per_step * args.steps}
+    del gG
 
     result = {
         "metric": METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
@@ -307,15 +300,16 @@ def run_ours(args):
                    "parallelism": f"replicas{world}" if world > 1 else "single",
                    "l2": "inputs larger than L2: 1.63 GB of weight digits rotated between re-uses of a matrix",
                    "per_step_bytes": step_bytes, "timing": "CUDA graph of one step (15 x digitize + GEMM), "
-                   "replayed --steps times; per-GEMM durations from timing events captured in the graphs",
-                   "ms_per_step_with_timing_events": round(ms_events, 4)},
+                   "replayed --steps times between two events",
+                   "gemm_ms_per_step": round(gemm_ms, 4)},
         "gpu_launches": launches["n"],
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "traffic": GEMM_TRAFFIC_PER_LAUNCH,
                      "algorithmic_bytes_per_launch": step_bytes // len(order), "peak_kind": peak_kind,
-                     "kernel": "k_exact_tc_i8: algorithmic bytes of the 15 decode GEMM launches / their summed "
-                               "event-timed durations (= per-launch average); traffic = ncu average per launch"},
-        "sweep_decode": per_gemm,
+                     "kernel": "k_exact_tc_i8: the step's 15 GEMM launches back to back in one CUDA graph on digits "
+                               "computed beforehand, replayed --steps times between two events; average launch "
+                               "duration = that time / 15, algorithmic bytes per launch = step bytes / 15; traffic "
+                               "= ncu average per launch"},
         "clocks": clk.summary(c0, c1),
     }
     e2e = e2e_bench(dev, W, order, args)  # every rank: whole-job end-to-end rate, max time over ranks
@@ -335,9 +329,10 @@ def run_ours(args):
         # CPU leg: the oracle checks the timed step's outputs (as the checker), then the CPU baseline is timed
         result["bitwise"] = bitwise_check(W, X, Y, order)
         result["bitwise_ok"] = result["bitwise"]["ok"]
+        if world == 1:
+            result["sweep_decode"] = decode_layers(dev, W, hbm, with_ref=not args.quick)
         if world == 1 and not args.quick:
-            result["ref_triton"] = ref_triton_decode(dev, W, hbm)
-            del W, X, Y
+            del W, X, Y, XD
             torch.cuda.empty_cache()
             result["decode_step"] = decode_step_bench(dev)
             result["cpu_baseline"] = cpu_baseline()
@@ -1009,6 +1004,9 @@ def run_case(args):
                                     out=y)
     elif kind == "step":
         print(json.dumps(decode_step_bench(dev)), flush=True)
+    elif kind == "layers":  # the chain-timed per-layer decode section of the default run alone
+        W = {name: make_weight_digits(K, N, 1000 + i, dev) for i, (name, K, N) in enumerate(SHAPES)}
+        print(json.dumps(decode_layers(dev, W, peaks()[0], with_ref=rest != ["noref"])), flush=True)
     elif kind == "attnbench":  # the attention section of the default run alone (BASELINE config 4 batches)
         print(json.dumps(attention_bench(dev, peaks()[0], False)), flush=True)
     elif kind == "attn":
@@ -1054,60 +1052,115 @@ REF_DECODE_CFGS = {1: [(16, 64, 256, 4, 3, 8, 4), (16, 128, 128, 4, 4, 8, 4), (1
                         (16, 64, 256, 4, 3, 8, 4), (64, 128, 128, 4, 4, 8, 1)]}
 
 
-def ref_triton_decode(dev, W, hbm, budget_s=150.0):
-    """The reference's own Triton exact GEMM (kernels.py:_exact_kernel / _exact_bf16_kernel + _exact_fin, from
-    baseline/_ref) against ours on the same B200 and the same digits, at the headline decode shapes. Both arms are
-    timed the same way: one CUDA graph per M holding the five GEMMs with timing events around each (weights rotate
-    through L2, so every GEMM streams its weights from HBM). For every shape the reference gets the best of its
-    B300-table and default tile configurations for that M, each with INT8 and with bf16 MMAs; each reference output is
-    also compared bitwise with ours. Stops adding candidates after `budget_s` seconds (Triton compiles each one)."""
+L2_BYTES = 126 * 1024 * 1024
+
+
+def _chain_time(op, R, stream, reps=5, warm=2):
+    """Capture op(0) .. op(R-1) back to back in one CUDA graph (no events between them, so each launch overlaps its
+    neighbours exactly as in a captured decode step), replay it `reps` times between two events, and return the
+    device time per op in microseconds."""
+    import torch
+    with torch.cuda.stream(stream):
+        for _ in range(warm):
+            for r in range(R):
+                op(r)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for r in range(R):
+            op(r)
+    with torch.cuda.stream(stream):
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+    torch.cuda.synchronize()
+    del g
+    return a.elapsed_time(b) * 1e3 / (reps * R)
+
+
+def decode_layers(dev, W, hbm, with_ref=True, budget_s=150.0):
+    """Per-layer decode figures of the headline shapes (M in {1, 16, 64}), every one timed as a chain: R ops back to
+    back in one CUDA graph, events only around the replays, time / R. The ops of a chain rotate over C copies of the
+    layer's weight digits with C x bytes >= 3 x L2, so every op streams its weights from HBM.
+
+    * op_us:   the exact linear as vLLM calls it (exactmm::linear = activation digitize + exact GEMM)
+    * gemm_us: the GEMM alone on pre-computed digits (k_exact_tc_i8 back to back); frac_hbm = its algorithmic bytes
+               (2NK + 4N + 2MK + 4M + 2MN) / gemm_us / the measured HBM peak
+    * ref_op_us (with_ref): the reference's own Triton op on the same B200 and the same inputs, timed the same way:
+      its digitize + exact_linear (kernels.py:74-85, :257-289: _digitize_kernel, _exact_kernel or _exact_bf16_kernel,
+      and _exact_fin for split-K), installed under baseline/_ref. It gets the best of the tile configurations of its
+      shipped B300 table and defaults for that M, each with INT8 and bf16 MMAs; its output is compared bitwise with
+      ours. Candidates stop after `budget_s` seconds of trying (Triton compiles each one).
+
+    A single kernel between two timing events costs several microseconds more than the same kernel in a chain (the
+    event pair alone, around an empty kernel, measured ~6 us on B200), which is why no figure here brackets single
+    launches with events."""
     import torch
     from vllm_exact import kernels as KK
-    try:
-        RK = _load_reference_module("kernels")
-    except SystemExit as e:
-        return {"unavailable": str(e)}
+    RK = None
+    if with_ref:
+        try:
+            RK = _load_reference_module("kernels")
+        except SystemExit as e:
+            RK = None
+            ref_missing = str(e)
     t_start = time.time()
     stream = torch.cuda.Stream(dev)
     res = {}
-    for M in DECODE_M:
-        xs = {name: KK.digitize(make_activation(M, K, 17 * M + i, dev), 14) for i, (name, K, N) in enumerate(SHAPES)}
-        ours_y = {name: torch.empty(M, N, device=dev, dtype=torch.bfloat16) for name, K, N in SHAPES}
-        KK.reserve_workspace(max(KK.lib().ex_linear_workspace_bytes(M, N, K, 0, 0) for _, K, N in SHAPES), dev,
-                             stream=stream)
-        fns = [(lambda n=name: KK.exact_linear(xs[n], W[n], 14, True, out=ours_y[n])) for name, K, N in SHAPES]
-        _, ours_ms = _graph_time(fns, 10, stream)
-        best = {}
-        for cfg in REF_DECODE_CFGS[M]:
-            for mma in (0, 1):
-                if time.time() - t_start > budget_s and best:
-                    break
-                c = cfg + (mma,)
-                ys = {name: torch.empty(M, N, device=dev, dtype=torch.bfloat16) for name, K, N in SHAPES}
-                rf = [(lambda n=name, c=c: RK.exact_linear(xs[n], W[n], 14, True, out=ys[n], cfg=c))
-                      for name, K, N in SHAPES]
-                try:
-                    _, ref_ms = _graph_time(rf, 5, stream)
-                except Exception as e:  # a configuration that does not compile here
-                    print(f"reference cfg {c} failed: {type(e).__name__}", file=sys.stderr)
-                    continue
-                for (name, K, N), ms in zip(SHAPES, ref_ms):
-                    same = bool(torch.equal(ys[name], ours_y[name]))
-                    prev = best.get(name)
-                    if prev is None or ms < prev[0]:
-                        best[name] = (ms, c, same and (prev is None or prev[2]))
-                    elif not same:
-                        best[name] = (prev[0], prev[1], False)
-        for (name, K, N), ms in zip(SHAPES, ours_ms):
-            if name not in best:
-                continue
-            rms, rc, same = best[name]
+    for i, (name, K, N) in enumerate(SHAPES):
+        by_w = 2 * N * K
+        C = max(1, -(-3 * L2_BYTES // by_w))
+        Wc = [W[name]] + [tuple(t.clone() for t in W[name]) for _ in range(C - 1)]
+        for w in Wc[1:]:
+            KK.mark_static(*w)
+        R = C * max(1, -(-8 // C))
+        for M in DECODE_M:
+            x = make_activation(M, K, 17 * M + i, dev)
+            xd = KK.digitize(x, 14)
+            xb = KK._alloc_digits(M, K, dev)
+            y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            KK.reserve_workspace(KK.lib().ex_linear_workspace_bytes(M, N, K, 0, 0), dev, stream=stream)
+            op_us = _chain_time(lambda r: KK.exact_linear(KK.digitize(x, 14, out=xb), Wc[r % C], 14, True, out=y),
+                                R, stream)
+            gemm_us = _chain_time(lambda r: KK.exact_linear(xd, Wc[r % C], 14, True, out=y), R, stream)
             by = gemm_bytes(M, K, N)
-            res[f"{name}/M{M}"] = {"ours_us": round(ms * 1e3, 2), "ref_us": round(rms * 1e3, 2),
-                                   "speedup": round(rms / ms, 3), "ours_frac_hbm": round(by / ms / 1e6 / hbm, 3),
-                                   "ref_frac_hbm": round(by / rms / 1e6 / hbm, 3), "ref_cfg": list(rc),
-                                   "bitwise_equal": same}
-        del xs, ours_y
+            row = {"op_us": round(op_us, 2), "gemm_us": round(gemm_us, 2), "GBps": round(by / gemm_us / 1e3, 1),
+                   "frac_hbm": round(by / gemm_us / 1e3 / hbm, 3)}
+            if with_ref and RK is None:
+                row["ref"] = ref_missing
+            elif RK is not None:
+                ours_y = y.clone()
+                rb = KK._alloc_digits(M, K, dev)
+                best = None
+                for cfg in REF_DECODE_CFGS[M]:
+                    for mma in (0, 1):
+                        if best is not None and time.time() - t_start > budget_s:
+                            break
+                        c = cfg + (mma,)
+                        yr = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+                        try:
+                            us = _chain_time(lambda r: RK.exact_linear(RK.digitize(x, 14, out=rb), Wc[r % C], 14,
+                                                                       True, out=yr, cfg=c), R, stream, reps=3)
+                        except Exception as e:  # a configuration that does not compile here
+                            print(f"reference cfg {c} failed: {type(e).__name__}", file=sys.stderr)
+                            continue
+                        same = bool(torch.equal(yr, ours_y))
+                        if best is None or us < best[0]:
+                            best = (us, c, same and (best is None or best[2]))
+                        elif not same:
+                            best = (best[0], best[1], False)
+                if best is not None:
+                    row.update({"ref_op_us": round(best[0], 2), "speedup_op": round(best[0] / op_us, 3),
+                                "ref_cfg": list(best[1]), "bitwise_equal": best[2]})
+            res[f"{name}/M{M}"] = row
+            del x, xd, xb, y
+        del Wc
+        torch.cuda.empty_cache()
     return res
 
 

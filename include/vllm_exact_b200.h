@@ -47,6 +47,14 @@ enum {
   EX_ALGO_TC_I8 = 2  /* tcgen05 kind::i8 tensor cores, TMA-fed, int32 accumulators in tensor memory */
 };
 
+/* Flag OR-ed into the `algo` argument of ex_linear, ex_linear_partial_i64 and ex_linear_noalloc: the weight digits
+ * (wh, wl) are static, i.e. written before `stream` was last synchronized. The tensor-core kernel then starts loading
+ * its first weight tiles before the kernels ahead of it on the stream have finished (programmatic dependent launch),
+ * instead of after. Same result bits. Do not set it while a kernel that writes the weight digits may still be running
+ * on the stream (for instance right after digitizing the weights without a synchronization). No counterpart in the
+ * reference (its Triton launches do not overlap). */
+#define EX_LINEAR_STATIC_WEIGHTS 0x100
+
 const char* ex_version(void);
 const char* ex_status_string(int status);
 /* Message of the last EX_ERR_CUDA on this host thread. */

@@ -6,8 +6,14 @@
 //   * every (m-tile, n-tile) has its K iterations [0, KI) covered exactly once (so each ticket reaches KI once);
 //   * a tile covered by more than one segment (a split tile) gets one workspace slot from all of its contributors,
 //     distinct split tiles get distinct slots, and the slot's accumulator and ticket lie inside the planned workspace;
-//   * a plan without workspace has no split tile; shared memory fits the 227 KB limit with at least two stages.
-// Prints "OK <plans> <segments>" or the first violation, and exits non-zero on a violation.
+//   * a plan without workspace has no split tile, unless it is a cluster plan; shared memory fits the 227 KB limit
+//     with at least two stages;
+//   * a cluster plan (cs > 1) has clusters of cs = ks x gs <= 8 consecutive CTAs, all of which fit on the device at
+//     once, one segment per CTA, and CTA rank p x gs + j of cluster t owns K part p (of ks equal parts) of n-tile t on
+//     m-tile j, so the cluster holds every K part of its gs tiles; its partial tile fits in the pipeline stages.
+// Plans are made for three device models: no cluster support, and two cluster capacity tables (every SM usable, and
+// SMs in groups of 18 as in graphics processing clusters).
+// Prints "OK <plans> <segments> <cluster plans>" or the first violation, and exits non-zero on a violation.
 #include <algorithm>
 #include <cstdio>
 #include <vector>
@@ -22,8 +28,9 @@ struct Fail {
   char msg[512];
 };
 
-bool check_plan(int64_t M, int64_t N, int64_t K, int split_k, int sms, long long& nseg, Fail& f) {
-  const TcPlan p = tc_plan(M, N, K, split_k, sms);
+bool check_plan(int64_t M, int64_t N, int64_t K, int split_k, int sms, const int* cap, long long& nseg,
+                long long& ncl, Fail& f) {
+  const TcPlan p = tc_plan(M, N, K, split_k, sms, cap);
   auto bad = [&](const char* what) {
     std::snprintf(f.msg, sizeof f.msg, "M=%lld N=%lld K=%lld split=%d sms=%d: %s", (long long)M, (long long)N,
                   (long long)K, split_k, sms, what);
@@ -38,6 +45,26 @@ bool check_plan(int64_t M, int64_t N, int64_t K, int split_k, int sms, long long
   if (p.m_tiles != (int)((M + p.BT - 1) / p.BT) || (int64_t)p.m_tiles * p.BT < M) return bad("m-tiles");
   if ((int64_t)p.n_tiles * 128 < N || (int64_t)p.KI * TC_BK < K) return bad("n-tiles / KI");
   if (p.stages < 2 || p.smem > 227 * 1024) return bad("shared memory");
+  if (p.cs > 1) {
+    ++ncl;
+    if (!cap) return bad("cluster plan without cluster support");
+    if (p.cs != p.ks * p.gs || p.cs > TC_MAX_CLUSTER || p.ks < 2 || p.G % p.cs != 0) return bad("cluster shape");
+    if ((int64_t)cap[p.cs] * p.cs < p.G) return bad("clusters do not fit at once");
+    if (p.chunks != 1 || p.ws_bytes != 0 || a.ks != p.ks) return bad("cluster plan fields");
+    if ((size_t)p.BT * 128 * 8 > (size_t)p.stages * tc_stage_bytes(p.BT)) return bad("partial tile exceeds stages");
+    for (int cta = 0; cta < p.G; ++cta) {
+      TcWalk w(a, cta);
+      TcSeg s;
+      if (!w.next(s)) return bad("cluster CTA without segment");
+      const int t = cta / p.cs, r = cta % p.cs, part = r / p.gs, j = r % p.gs;
+      if (s.n_tile != t || s.m_tile != j) return bad("cluster CTA on another tile");
+      if (s.kb != (int)((int64_t)p.KI * part / p.ks) || s.ke != (int)((int64_t)p.KI * (part + 1) / p.ks))
+        return bad("cluster CTA K part");
+      if (w.next(s)) return bad("cluster CTA with two segments");
+    }
+  } else if (a.ks != 0) {
+    return bad("cluster reduction flag outside a cluster plan");
+  }
   const size_t tiles = (size_t)p.m_tiles * p.n_tiles;
   std::vector<std::vector<std::pair<int, int>>> cov(tiles);
   std::vector<long long> slot_of(tiles, -1);
@@ -52,6 +79,7 @@ bool check_plan(int64_t M, int64_t N, int64_t K, int split_k, int sms, long long
       const size_t t = (size_t)s.m_tile * p.n_tiles + s.n_tile;
       cov[t].push_back({s.kb, s.ke});
       if (s.kb == 0 && s.ke == p.KI) continue;
+      if (p.cs > 1) continue;  // reduced inside the cluster
       const long long sl = tc_split_slot(a, s.n_tile, s.m_tile);
       if (sl < 0 || sl >= slots) return bad("split slot out of range");
       if (slot_of[t] < 0) slot_of[t] = sl;
@@ -71,6 +99,7 @@ bool check_plan(int64_t M, int64_t N, int64_t K, int split_k, int sms, long long
       k = seg.second;
     }
     if (k != p.KI) return bad("tile not covered to KI");
+    if (v.size() > 1 && p.cs > 1) continue;
     if (v.size() > 1) {
       if (slot_of[t] < 0) return bad("split tile without slot");
       used.push_back(slot_of[t]);
@@ -91,19 +120,24 @@ int main() {
   const int64_t Ks[] = {1, 100, 128, 1024, 4096, 12288, 65536};
   const int splits[] = {0, 1, 2, 3, 4, 8};
   const int smss[] = {148, 132, 7, 2, 1};
-  long long plans = 0, nseg = 0;
+  long long plans = 0, nseg = 0, ncl = 0;
   Fail f;
-  for (int64_t M : Ms)
-    for (int64_t N : Ns)
-      for (int64_t K : Ks)
-        for (int sk : splits)
-          for (int sms : smss) {
-            ++plans;
-            if (!check_plan(M, N, K, sk, sms, nseg, f)) {
-              std::printf("FAIL %s\n", f.msg);
-              return 1;
+  for (int model = 0; model < 3; ++model)
+    for (int sms : smss) {
+      int cap[TC_MAX_CLUSTER + 1] = {};
+      for (int c = 2; c <= TC_MAX_CLUSTER; ++c)
+        cap[c] = model == 1 ? sms / c : (sms / 18) * (18 / c) + (sms % 18) / c;
+      for (int64_t M : Ms)
+        for (int64_t N : Ns)
+          for (int64_t K : Ks)
+            for (int sk : splits) {
+              ++plans;
+              if (!check_plan(M, N, K, sk, sms, model == 0 ? nullptr : cap, nseg, ncl, f)) {
+                std::printf("FAIL %s\n", f.msg);
+                return 1;
+              }
             }
-          }
-  std::printf("OK %lld %lld\n", plans, nseg);
+    }
+  std::printf("OK %lld %lld %lld\n", plans, nseg, ncl);
   return 0;
 }

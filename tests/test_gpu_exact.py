@@ -249,8 +249,9 @@ def test_workspace_growth_during_graph_capture(K):
     """vLLM captures decode graphs for several batch sizes on one stream. When a later capture needs a larger split-K
     workspace, the workspace grows during capture; the one an earlier graph captured must stay valid (it is kept
     alive, never freed). Capture small-then-large on a fresh stream, replay both graphs alternately with new inputs,
-    and compare every output with an eager call."""
-    Kd, N = 4096, 4096
+    and compare every output with an eager call. (N = 24576: wide enough that these plans reduce split tiles through
+    the workspace rather than inside thread-block clusters.)"""
+    Kd, N = 4096, 24576
     w = torch.randn(N, Kd, generator=torch.Generator().manual_seed(5)) * 0.02
     wd = K.digitize(w.bfloat16().to(DEV), 14)
     st = torch.cuda.Stream()
@@ -279,3 +280,50 @@ def test_workspace_growth_during_graph_capture(K):
             torch.cuda.synchronize()
             assert torch.equal(ys[m], ref), (r, m)
     del graphs
+
+
+@pytest.mark.parametrize("M,N,Kd", [(1, 4096, 4096), (16, 6144, 4096), (64, 4096, 12288), (64, 24576, 4096),
+                                    (256, 4096, 4096), (300, 1000, 1024)])
+def test_static_weights_same_bits(K, M, N, Kd):
+    """Weight digits marked static (digitize_weight -> EX_LINEAR_STATIC_WEIGHTS: the GEMM starts loading its first
+    weight tiles before the kernels ahead of it have finished) give the same bits as unmarked digits of the same
+    weights, eagerly and in a CUDA graph of back-to-back ops (digitize + GEMM, four weight matrices in turn) where
+    every GEMM's early loads overlap the kernels before it. Shapes cover cluster-reduced, workspace-reduced and
+    whole-tile plans."""
+    g = torch.Generator().manual_seed(M + N + Kd)
+    ws = [(torch.randn(N, Kd, generator=g) * 0.02).bfloat16().to(DEV) for _ in range(4)]
+    wd_static = [K.digitize_weight(w, 14) for w in ws]
+    wd_plain = [K.digitize(w, 14) for w in ws]
+    assert all(K.is_static(d[0], d[1]) for d in wd_static)
+    assert not any(K.is_static(d[0], d[1]) for d in wd_plain)
+    xs = []
+    for r in range(4):
+        x = torch.randn(M, Kd, generator=g)
+        x[torch.rand(M, Kd, generator=g) < 0.001] *= 50
+        xs.append(x.bfloat16().to(DEV))
+    ref = [K.exact_linear(K.digitize(x, 14), wd, 14, True, out=torch.empty(M, N, device=DEV, dtype=torch.bfloat16))
+           for x, wd in zip(xs, wd_plain)]
+    for x, wd, y0 in zip(xs, wd_static, ref):
+        y = K.exact_linear(K.digitize(x, 14), wd, 14, True, out=torch.empty_like(y0))
+        assert torch.equal(y, y0)
+    st = torch.cuda.Stream()
+    outs = [torch.empty_like(y0) for y0 in ref]
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        for x, wd, y in zip(xs, wd_static, outs):  # warm-up (workspace of `st`) outside the capture
+            K.exact_linear(K.digitize(x, 14), wd, 14, True, out=y)
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=st):
+        for x, wd, y in zip(xs, wd_static, outs):
+            K.exact_linear(K.digitize(x, 14), wd, 14, True, out=y)
+    for _ in range(3):
+        for y in outs:
+            y.fill_(float("nan"))
+        gr.replay()
+        torch.cuda.synchronize()
+        for y, y0 in zip(outs, ref):
+            assert torch.equal(y, y0)
+    del gr
+    from vllm_exact import _lib
+    assert _lib.device_error() == 0

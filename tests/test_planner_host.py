@@ -1,7 +1,8 @@
 """CPU check of the tensor-core GEMM's work plan: tests/planner_check.cpp is compiled with g++ against the planner
-header the kernel itself uses (vllm-exact_b200/csrc/ex_tc_plan.h) and enumerates 28,350 plans (token tiles, group
-partitions, explicit split-K, SM counts from 1 to 148): every tile's K range covered exactly once, one
-distinct in-bounds workspace slot per split tile. These properties are why every partition gives identical bits."""
+header the kernel itself uses (vllm-exact_b200/csrc/ex_tc_plan.h) and enumerates 85,050 plans (token tiles, group
+partitions, explicit split-K, SM counts from 1 to 148, three cluster-capacity models): every tile's K range covered
+exactly once, one distinct in-bounds workspace slot per split tile, and in cluster plans every K part of a tile held
+by one cluster. These properties are why every partition gives identical bits."""
 import shutil
 import subprocess
 from pathlib import Path
@@ -21,5 +22,5 @@ def test_tc_plan_covers_every_tile_exactly_once(tmp_path):
                    check=True, capture_output=True, text=True, timeout=300)
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout + r.stderr
-    word, plans, segments = r.stdout.split()
-    assert word == "OK" and int(plans) == 28350 and int(segments) > 5_000_000
+    word, plans, segments, cluster_plans = r.stdout.split()
+    assert word == "OK" and int(plans) == 85050 and int(segments) > 15_000_000 and int(cluster_plans) > 1000

@@ -54,8 +54,9 @@ def _with_workspace(L, xd, wd, out, algo=0, split_k=0):
                        out.stride(0), ws.data_ptr(), need, split_k, algo, torch.cuda.current_stream().cuda_stream)
 
 
-@pytest.mark.parametrize("M,N,Kd,algo,split_k", [(64, 4096, 4096, 0, 0),    # tensor cores, split tiles
+@pytest.mark.parametrize("M,N,Kd,algo,split_k", [(64, 4096, 4096, 0, 0),    # tensor cores, cluster-reduced split
                                                  (16, 6144, 4096, 0, 0),
+                                                 (64, 24576, 4096, 0, 0),   # tensor cores, split tiles in scratch
                                                  (5, 1000, 12288, 2, 4),    # tensor cores, explicit split
                                                  (7, 300, 2048, 1, 4)])     # SIMT, explicit split
 def test_noalloc_matches_workspace_entry_point(env, M, N, Kd, algo, split_k):
@@ -79,7 +80,7 @@ def test_noalloc_recovers_from_dirty_scratch(env):
     call then goes wrong, and that ex_linear_noalloc_reset brings back the exact bits on two calls in a row."""
     lib, K = env
     L = lib.lib()
-    M, N, Kd = 64, 4096, 4096  # the automatic tensor-core plan splits every tile four ways: scratch in use
+    M, N, Kd = 64, 24576, 4096  # the automatic tensor-core plan splits tiles across CTAs through the scratch
     assert L.ex_linear_workspace_bytes(M, N, Kd, 0, lib.EX_ALGO_TC_I8) > 0
     xd, wd = _inputs(K, M, N, Kd, seed=7)
     ref = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)

@@ -144,7 +144,8 @@ int linear_impl(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* 
   if (!PARTIAL && (!sx || !sw)) return EX_ERR_ARG;
   if (!PARTIAL && !dtype_ok(out_dtype)) return EX_ERR_DTYPE;
   if (split_k < 0) return EX_ERR_ARG;
-  algo = pick_algo(algo, xh, xl, ldx, wh, wl, ldw, M, N, K);
+  const bool static_w = (algo & EX_LINEAR_STATIC_WEIGHTS) != 0;
+  algo = pick_algo(algo & ~EX_LINEAR_STATIC_WEIGHTS, xh, xl, ldx, wh, wl, ldw, M, N, K);
   if (algo == EX_ALGO_SIMT) {
     const SimtPlan p = simt_plan(M, N, K, split_k);
     if (p.ws_bytes > 0 && (!workspace || workspace_bytes < p.ws_bytes)) return EX_ERR_WORKSPACE;
@@ -154,11 +155,11 @@ int linear_impl(const int8_t* xh, const int8_t* xl, int64_t ldx, const int32_t* 
   }
   if (algo == EX_ALGO_TC_I8) {
     if (!ex::tc_supported(xh, xl, ldx, wh, wl, ldw, M, N, K)) return EX_ERR_ALIGN;
-    const ex::TcPlan p = ex::tc_plan(M, N, K, split_k, num_sms());
+    const ex::TcPlan p = ex::tc_plan(M, N, K, split_k, num_sms(), ex::tc_cluster_cap());
     if (p.ws_bytes > 0 && (!workspace || workspace_bytes < p.ws_bytes)) return EX_ERR_WORKSPACE;
     if (p.ws_bytes > 0 && reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return EX_ERR_ALIGN;
     cudaError_t e = ex::launch_tc<PARTIAL>(p, F, trunc, out_dtype, xh, xl, ldx, cx, sx, wh, wl, ldw, cw, sw, (int)M,
-                                           (int)N, (int)K, out, ldo, workspace, st);
+                                           (int)N, (int)K, out, ldo, workspace, static_w, st);
     if (e == cudaErrorNotSupported) return EX_ERR_UNSUPPORTED;
     return cuda_status(e);
   }
@@ -241,9 +242,10 @@ int launch_merge(const float* ws_m, const float* ws_l, const float* ws_acc, void
 
 size_t linear_ws(int64_t M, int64_t N, int64_t K, int split_k, int algo) {
   if (M <= 0 || N <= 0) return 0;
+  algo &= ~EX_LINEAR_STATIC_WEIGHTS;
   size_t a = simt_plan(M, N, K, split_k).ws_bytes;
   if (algo == EX_ALGO_SIMT) return a;
-  const size_t b = ex::tc_plan(M, N, K, split_k, num_sms()).ws_bytes;
+  const size_t b = ex::tc_plan(M, N, K, split_k, num_sms(), ex::tc_cluster_cap()).ws_bytes;
   if (algo == EX_ALGO_TC_I8) return b;
   return std::max(a, b);  // automatic choice: enough for either algorithm
 }
@@ -338,12 +340,12 @@ int ex_linear_noalloc(const int8_t* xh, const int8_t* xl, int64_t ldx, const int
   int rc = check_linear_args(xh, xl, ldx, cx, wh, wl, ldw, cw, M, N, K, F, out, ldo);
   if (rc != EX_OK || M == 0 || N == 0) return rc;
   if (split_k < 0) return EX_ERR_ARG;
-  const int chosen = pick_algo(algo, xh, xl, ldx, wh, wl, ldw, M, N, K);
+  const int chosen = pick_algo(algo & ~EX_LINEAR_STATIC_WEIGHTS, xh, xl, ldx, wh, wl, ldw, M, N, K);
   size_t need = 0;
   if (chosen == EX_ALGO_SIMT)
     need = simt_plan(M, N, K, split_k).ws_bytes;
   else if (chosen == EX_ALGO_TC_I8 && ex::tc_supported(xh, xl, ldx, wh, wl, ldw, M, N, K))
-    need = ex::tc_plan(M, N, K, split_k, num_sms()).ws_bytes;
+    need = ex::tc_plan(M, N, K, split_k, num_sms(), ex::tc_cluster_cap()).ws_bytes;
   if (need > EX_NOALLOC_SCRATCH_BYTES) {
     g_last_error = "ex_linear_noalloc: this shape's split-K plan needs " + std::to_string(need) +
                    " bytes of scratch, more than the static EX_NOALLOC_SCRATCH_BYTES (" +

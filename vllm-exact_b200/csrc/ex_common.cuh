@@ -251,6 +251,40 @@ __device__ __forceinline__ uint32_t elect_one() {
 }
 
 // ------------------------------------------------------------------------------------------------------------------
+// thread-block clusters: rank, distributed shared memory, cluster-wide barrier
+// ------------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address in the shared memory of cluster CTA `rank` of the variable at local shared address `addr`.
+__device__ __forceinline__ uint32_t dsmem_map(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+// (no memory clobber: these loads follow a cluster barrier, which orders them, and may overlap one another)
+__device__ __forceinline__ long long dsmem_ld_s64(uint32_t addr) {
+  long long v;
+  asm volatile("ld.shared::cluster.s64 %0, [%1];" : "=l"(v) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ void dsmem_ld_v2s64(uint32_t addr, long long& a, long long& b) {
+  asm volatile("ld.shared::cluster.v2.s64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(addr) : "memory");
+}
+
+// Every thread of every CTA of the cluster arrives (release) and waits (acquire): shared-memory writes made before
+// the barrier by any CTA of the cluster are visible to all of them after it. Not a software spin: the hardware
+// completes it once all threads have arrived, so every thread must reach it exactly as often as the others.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// ------------------------------------------------------------------------------------------------------------------
 // Launch with the programmatic-stream-serialization attribute: the kernel may start while the previous kernel in the
 // stream is finishing; it must call pdl_wait() before touching memory that kernel produces or consumes.
 // ------------------------------------------------------------------------------------------------------------------
@@ -267,6 +301,27 @@ static cudaError_t ex_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// The same launch as a grid of thread-block clusters of `cluster` CTAs along x (gridDim.x a multiple of it).
+template <typename... KArgs, typename... Args>
+static cudaError_t ex_launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, int cluster,
+                                         cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = (unsigned)cluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 

@@ -21,12 +21,18 @@
 // Work partition: the (n-tile, k-iteration) space of one row of m-tiles is cut into `groups` equal contiguous
 // ranges; a group is gs sibling CTAs that walk the same range on gs different m-tiles in lockstep, so each weight
 // tile leaves HBM once and the siblings find it in L2. A CTA's walk is a list of segments (m-tile, n-tile, k_begin,
-// k_end). A segment covering a whole tile is finished straight from TMEM; otherwise its int64 totals are added with
-// bulk reduce-adds (TMA engine) into the tile's workspace slot (one slot per (group boundary, m-tile)) and a ticket
-// counting k-iterations elects the CTA that completes the tile, which applies the epilogue and zeroes the slot
-// again. Integer addition is exact and order-free, so the result bits do not depend on the partition or on arrival
-// order.
+// k_end). A segment covering a whole tile is finished straight from TMEM. Split tiles are combined in one of two ways:
+//   * cluster reduction (plans that cut every n-tile into ks equal K parts, one per CTA): the CTAs of one n-tile are a
+//     thread-block cluster; each writes its int64 partial tile to its own shared memory, and after a cluster barrier
+//     each adds a 1/ks share of the tile's elements over the ks CTAs through distributed shared memory and finishes
+//     it. No global workspace, no atomics;
+//   * workspace reduction (other plans): int64 totals are added with bulk reduce-adds (TMA engine) into the tile's
+//     workspace slot (one slot per (group boundary, m-tile)) and a ticket counting k-iterations elects the CTA that
+//     completes the tile, which applies the epilogue and zeroes the slot again.
+// Integer addition is exact and order-free, so the result bits do not depend on the partition or on arrival order.
 #pragma once
+#include <mutex>
+
 #include "ex_common.cuh"
 #include "ex_tc_plan.h"
 
@@ -76,6 +82,25 @@ __device__ __forceinline__ void tc_finish_chunk(const long long (&tot)[CW], int 
     for (int j = 0; j < CW; ++j)
       if (j < jmax) op[(int64_t)j * a.ldo] = __float2half_rn(f[j]);
   }
+}
+
+// One output element (token m, weight row n) from its int64 total and the scale words of its token (sxm, cxm) and
+// weight row (swn, cwn): the same arithmetic as tc_finish_chunk.
+__device__ __forceinline__ void tc_finish_one(long long tot, int m, int n, int sxm, int cxm, int swn, long long cwn,
+                                              const TcArgs& a) {
+  if (a.F == 15) tot += 128ll * ((long long)cxm + cwn) + 16384ll * (long long)a.K;
+  const int64_t idx = (int64_t)m * a.ldo + n;
+  if (a.partial) {
+    reinterpret_cast<long long*>(a.out)[idx] = tot;
+    return;
+  }
+  const float f = ex_scale_to_f32(tot, sxm, swn);
+  if (a.out_dtype == EX_DTYPE_BF16)
+    reinterpret_cast<__nv_bfloat16*>(a.out)[idx] = __float2bfloat16_rn(f);
+  else if (a.out_dtype == EX_DTYPE_F32)
+    reinterpret_cast<float*>(a.out)[idx] = f;
+  else
+    reinterpret_cast<__half*>(a.out)[idx] = __float2half_rn(f);
 }
 
 template <int CW>
@@ -154,25 +179,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  // Programmatic dependent launch: this prologue may overlap the previous kernel (typically the activation
-  // digitizer). Before waiting, only warm L2 with this CTA's first weight tiles (L2 is coherent with any writer, so
-  // this is safe even if the previous kernel wrote them); every shared-memory load, every read of activations or
-  // scales and every write happens after pdl_wait().
+  // Programmatic dependent launch: this prologue may overlap the kernels still running before it (typically the
+  // activation digitizer and the previous GEMM). Before waiting, the producer touches only this CTA's first S weight
+  // tiles: with a.w_early (the caller guarantees the weight digits are static, i.e. written before the stream was
+  // last synchronized) it loads them into the first S pipeline stages, so the weight stream starts at once;
+  // otherwise it only warms L2 with them (L2 is coherent with any writer, so that is safe even if a kernel still
+  // running wrote them). Activation tiles, scales and every write wait for pdl_wait().
+  int pre = 0;  // producer lane: pipeline stages whose weight tiles were loaded before pdl_wait()
   if (warp == 0 && lane == 0) {
+    const uint64_t pol_w = l2_policy_evict_first();
     TcWalk walk(a, (int)blockIdx.x);
     TcSeg sg;
-    int left = S;
-    while (left > 0 && walk.next(sg)) {
-      const int n_tile = sg.n_tile;
-      for (int kt = sg.kb; kt < sg.ke && left > 0; ++kt, --left) {
-        tma_prefetch_l2_2d(&tm_wh, kt * TC_BK, n_tile * Lay::WROWS);
-        tma_prefetch_l2_2d(&tm_wl, kt * TC_BK, n_tile * Lay::WROWS);
+    while (pre < S && walk.next(sg)) {
+      const int wr = sg.n_tile * Lay::WROWS;
+      for (int kt = sg.kb; kt < sg.ke && pre < S; ++kt, ++pre) {
+        if (a.w_early) {
+          uint8_t* st = smem + (size_t)pre * Lay::STAGE;
+          mbar_arrive_expect_tx(full_bar + pre, Lay::STAGE);  // this stage's activation tiles complete it later
+          tma_load_2d(st, &tm_wh, full_bar + pre, kt * TC_BK, wr, pol_w);
+          tma_load_2d(st + TC_WTILE, &tm_wl, full_bar + pre, kt * TC_BK, wr, pol_w);
+        } else {
+          tma_prefetch_l2_2d(&tm_wh, kt * TC_BK, wr);
+          tma_prefetch_l2_2d(&tm_wl, kt * TC_BK, wr);
+        }
       }
     }
+    if (!a.w_early) pre = 0;
   }
   pdl_launch_dependents();
   pdl_wait();
 
+  int fin_sw = 0;        // cluster reduction: scale words of the weight row this thread finishes
+  long long fin_cw = 0;
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
@@ -187,16 +225,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       while (ok && walk.next(sg)) {
         const int n_tile = sg.n_tile, m_tile = sg.m_tile;
         for (int kt = sg.kb; kt < sg.ke; ++kt) {
-          if (!mbar_wait(empty_bar + stage, phase ^ 1, EX_DEVERR_WAIT_SLOT)) {
+          const bool early = issued < pre;  // weights already loading into this stage since before pdl_wait()
+          if (!early && !mbar_wait(empty_bar + stage, phase ^ 1, EX_DEVERR_WAIT_SLOT)) {
             ok = false;
             break;
           }
           uint8_t* st = smem + (size_t)stage * Lay::STAGE;
           const int kc = kt * TC_BK;
           const int wr = n_tile * Lay::WROWS, xr = m_tile * BT;
-          mbar_arrive_expect_tx(full_bar + stage, Lay::STAGE);
-          tma_load_2d(st, &tm_wh, full_bar + stage, kc, wr, pol_w);
-          tma_load_2d(st + TC_WTILE, &tm_wl, full_bar + stage, kc, wr, pol_w);
+          if (!early) {
+            mbar_arrive_expect_tx(full_bar + stage, Lay::STAGE);
+            tma_load_2d(st, &tm_wh, full_bar + stage, kc, wr, pol_w);
+            tma_load_2d(st + TC_WTILE, &tm_wl, full_bar + stage, kc, wr, pol_w);
+          }
           tma_load_2d(st + 2 * TC_WTILE, &tm_xh, full_bar + stage, kc, xr, pol_x);
           tma_load_2d(st + 2 * TC_WTILE + Lay::XH, &tm_xl, full_bar + stage, kc, xr, pol_x);
           ++issued;
@@ -286,10 +327,50 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     constexpr int NCH = BT / CW;          // chunks per tile; this warp takes chunks half, half + 2, ...
     uint32_t nbulk = 0;  // bulk reduce-adds issued by this warp (selects and recycles the staging buffers)
     TcWalk walk(a, (int)blockIdx.x);
-    TcSeg sg;
+    TcSeg sg = {0, 0, 0, 0};
     int seg_i = 0;
     uint32_t epi_phase = 0;
-    while (walk.next(sg)) {
+    if (a.ks > 1) {
+      // Cluster reduction, first half: this CTA's only segment is one K part of its tile. Its int64 partial tile goes
+      // to this CTA's shared memory as [token][128 rows], over the pipeline stages: once the accumulator is complete
+      // every load has landed and every MMA has read its operands, so nothing touches that memory any more. The
+      // cluster's CTAs add the parts after the cluster barrier that follows the role branches.
+      long long* red = reinterpret_cast<long long*>(smem);
+      if (walk.next(sg)) {
+        // scale words the finishing step needs, fetched while the MMAs still run: the tile's token shifts and row
+        // sums into shared memory (one copy per CTA), this thread's weight row's into registers
+        const int m0 = sg.m_tile * BT;
+        for (int j = et; j < BT; j += 32 * TC_EPI_WARPS) {
+          const int t = min(m0 + j, a.M - 1);
+          tok_words[j] = a.partial ? 0 : __ldg(a.sx + t);
+          tok_words[128 + j] = a.F == 15 ? __ldg(a.cx + t) : 0;
+        }
+        const int part = (int)cluster_ctarank() / a.gs;
+        const int E = min(BT, a.M - m0) * 128;
+        const int nf = sg.n_tile * Lay::WROWS + (((int)(((int64_t)E * part) / a.ks) + et) & 127);
+        if (nf < a.N) {
+          fin_sw = a.partial ? 0 : __ldg(a.sw + nf);
+          fin_cw = a.F == 15 ? (long long)__ldg(a.cw + nf) : 0ll;
+        }
+      }
+      if (sg.kb < sg.ke && mbar_wait(tfull_bar, 0, EX_DEVERR_WAIT_MMA)) {
+        tc_fence_after();
+        const uint32_t t_hh = tmem_base + lane_off;
+#pragma unroll 1
+        for (int ci = half; ci < NCH; ci += 2) {
+          const int c = ci * CW;
+          uint32_t vh[CW], vm[CW], vl[CW];
+          tmem_ldc<CW>(t_hh + c, vh);
+          tmem_ldc<CW>(t_hh + BT + c, vm);
+          if (!a.trunc) tmem_ldc<CW>(t_hh + 2 * BT + c, vl);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < CW; ++j)
+            red[(c + j) * 128 + row] = ex_combine((int)vh[j], (int)vm[j], a.trunc ? 0 : (int)vl[j]);
+        }
+      }
+    }
+    while (a.ks <= 1 && walk.next(sg)) {
       const int buf = nbuf == 2 ? (seg_i & 1) : 0;
       const uint32_t use = nbuf == 2 ? (uint32_t)(seg_i >> 1) : (uint32_t)seg_i;
       const int n_tile = sg.n_tile, m_tile = sg.m_tile;
@@ -405,6 +486,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncwarp();
   }
 
+  if (a.ks > 1) {
+    // Cluster reduction, second half. Every thread of the cluster passes both barriers exactly once, on every path.
+    cluster_sync_all();  // all K parts of the tile are in their CTAs' shared memory
+    if (warp >= 2) {
+      // The ks CTAs of sibling m-tile j (cluster ranks p * gs + j) share the tile's valid elements (token-major,
+      // tokens < M only) in ks equal ranges; this CTA adds the ks parts of its range from distributed shared memory
+      // in a fixed order and finishes them. Consecutive threads take consecutive weight rows: coalesced stores.
+      // The element stride (256) is a multiple of 128, so each thread keeps one weight row n (its scale words were
+      // loaded before the barrier) and steps over tokens.
+      const int rank = (int)cluster_ctarank();
+      const int part = rank / a.gs, sib = rank % a.gs;
+      const int n_tile = (int)blockIdx.x / (a.ks * a.gs);
+      const int m0 = sib * BT;
+      const int E = min(BT, a.M - m0) * 128;
+      const int e0 = (int)(((int64_t)E * part) / a.ks), e1 = (int)(((int64_t)E * (part + 1)) / a.ks);
+      const int et = threadIdx.x - 64;
+      const int n = n_tile * 128 + ((e0 + et) & 127);
+      if (n < a.N) {
+        const uint32_t red_local = ex_smem_u32(smem);
+        uint32_t peer[TC_MAX_CLUSTER];
+#pragma unroll
+        for (int p = 0; p < TC_MAX_CLUSTER; ++p)
+          peer[p] = p < a.ks ? dsmem_map(red_local, (uint32_t)(p * a.gs + sib)) : 0u;
+#pragma unroll 4
+        for (int e = e0 + et; e < e1; e += 32 * TC_EPI_WARPS) {
+          long long v = 0;
+#pragma unroll
+          for (int p = 0; p < TC_MAX_CLUSTER; ++p)
+            if (p < a.ks) v += dsmem_ld_s64(peer[p] + (uint32_t)e * 8u);
+          const int tok = e >> 7;
+          tc_finish_one(v, m0 + tok, n, tok_words[tok], tok_words[128 + tok], fin_sw, fin_cw, a);
+        }
+      }
+    }
+    cluster_sync_all();  // no CTA leaves while another may still read its shared memory
+  }
+
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -448,6 +566,46 @@ static bool device_is_sm100() {
   return cached == 1;
 }
 
+// How many thread-block clusters of c CTAs of the tensor-core kernel (full shared-memory budget, one CTA per SM) the
+// current device holds at once, for c = 0 .. TC_MAX_CLUSTER (0 where clusters of c cannot run). Queried once per
+// device; nullptr when the query is not possible (no device), in which case plans use no clusters.
+static const int* tc_cluster_cap() {
+  static int cap[16][TC_MAX_CLUSTER + 1];
+  static int state[16] = {};  // 0 not queried, 1 ok, 2 failed
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 16) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (state[dev] == 0) {
+    state[dev] = 2;
+    if (cudaFuncSetAttribute(k_exact_tc_i8<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_BUDGET) ==
+        cudaSuccess) {
+      state[dev] = 1;
+      for (int c = 0; c <= TC_MAX_CLUSTER; ++c) {
+        cap[dev][c] = 0;
+        if (c < 2) continue;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(c * 64);
+        cfg.blockDim = dim3(TC_THREADS);
+        cfg.dynamicSmemBytes = TC_SMEM_BUDGET;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = (unsigned)c;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, k_exact_tc_i8<8>, &cfg) == cudaSuccess) cap[dev][c] = n;
+        else (void)cudaGetLastError();
+      }
+    } else {
+      (void)cudaGetLastError();
+    }
+  }
+  return state[dev] == 1 ? cap[dev] : nullptr;
+}
+
 // TMA rules: 16-byte aligned bases and leading dimensions (bytes); K within the int32-exact range.
 static bool tc_supported(const int8_t* xh, const int8_t* xl, int64_t ldx, const int8_t* wh, const int8_t* wl,
                          int64_t ldw, int64_t M, int64_t N, int64_t K) {
@@ -478,6 +636,9 @@ static cudaError_t launch_tc_bt(const TcPlan& p, const TcArgs& a, const CUtensor
                                 const CUtensorMap& mxh, const CUtensorMap& mxl, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(k_exact_tc_i8<BT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
   if (e != cudaSuccess) return e;
+  if (p.cs > 1)
+    return ex_launch_pdl_cluster(k_exact_tc_i8<BT>, dim3(p.G), dim3(TC_THREADS), p.smem, p.cs, st, mwh, mwl, mxh, mxl,
+                                 a);
   return ex_launch_pdl(k_exact_tc_i8<BT>, dim3(p.G), dim3(TC_THREADS), p.smem, st, mwh, mwl, mxh, mxl, a);
 }
 
@@ -485,7 +646,7 @@ template <bool PARTIAL>
 static cudaError_t launch_tc(const TcPlan& p, int F, int trunc, int out_dtype, const int8_t* xh, const int8_t* xl,
                              int64_t ldx, const int32_t* cx, const int32_t* sx, const int8_t* wh, const int8_t* wl,
                              int64_t ldw, const int32_t* cw, const int32_t* sw, int M, int N, int K, void* out,
-                             int64_t ldo, void* ws, cudaStream_t st) {
+                             int64_t ldo, void* ws, bool static_weights, cudaStream_t st) {
   CUtensorMap mwh, mwl, mxh, mxl;
   if (!encode_2d_i8(&mwh, wh, K, N, ldw, TC_BK, 128) || !encode_2d_i8(&mwl, wl, K, N, ldw, TC_BK, 128) ||
       !encode_2d_i8(&mxh, xh, K, M, ldx, TC_BK, p.BT) || !encode_2d_i8(&mxl, xl, K, M, ldx, TC_BK, p.BT))
@@ -507,6 +668,7 @@ static cudaError_t launch_tc(const TcPlan& p, int F, int trunc, int out_dtype, c
   a.out_dtype = out_dtype;
   a.partial = PARTIAL ? 1 : 0;
   tc_plan_args(p, a);
+  a.w_early = static_weights ? 1 : 0;
   switch (p.BT) {
     case 8: return launch_tc_bt<8>(p, a, mwh, mwl, mxh, mxl, st);
     case 16: return launch_tc_bt<16>(p, a, mwh, mwl, mxh, mxl, st);

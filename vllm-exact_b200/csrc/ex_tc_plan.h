@@ -5,6 +5,13 @@
 // kernel walks with TcWalk and tc_split_slot(), and a host test enumerates the same functions over many shapes and
 // SM counts to check that every (m-tile, n-tile) has its K range covered exactly once. That coverage is what makes
 // results bit-identical under any partition, because integer addition is exact and order-free.
+//
+// Split tiles are combined in one of two ways:
+//   * cluster reduction (TcPlan::cs > 1): when every n-tile is cut into s equal K parts and each CTA owns exactly one
+//     part of one tile, the s x gs CTAs of one n-tile form a thread-block cluster and add their int64 partial tiles
+//     through distributed shared memory; no global workspace is used;
+//   * workspace reduction (otherwise): bulk reduce-adds into a per-tile workspace slot in global memory, and a ticket
+//     elects the CTA that finishes the tile.
 #pragma once
 #include <algorithm>
 #include <cstddef>
@@ -40,6 +47,8 @@ struct TcPlan {
   int chunks;    // passes over the range: m-tiles c*gs + j for c < chunks
   int G;         // CTAs = groups * gs
   int stages;
+  int cs;        // CTAs per thread-block cluster (1: no cluster, split tiles reduced through the workspace)
+  int ks;        // K parts per n-tile reduced inside a cluster (cluster plans only; cs = ks * gs)
   size_t smem;
   size_t ws_bytes;
   size_t cnt_bytes;
@@ -60,6 +69,8 @@ struct TcArgs {
   int64_t T;  // n_tiles * KI
   int gs, groups, chunks;
   int stages;
+  int ks;  // > 1: cluster reduction of the ks K parts of each tile (CTA rank in the cluster = part * gs + sibling)
+  int w_early;  // 1: weight digits are static, so the first stages' weight tiles may load before griddepcontrol.wait
 };
 
 struct TcSeg {
@@ -137,8 +148,12 @@ inline int tc_pick_bt(int64_t M) {
 
 inline size_t tc_stage_bytes(int BT) { return 2 * (size_t)TC_WTILE + 2 * (size_t)BT * TC_BK; }
 
-// Single CTAs on 128-row n-tiles with the token tile picked from M.
-inline TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int split_k, int sms) {
+constexpr int TC_MAX_CLUSTER = 8;  // portable cluster size limit
+
+// Single CTAs on 128-row n-tiles with the token tile picked from M. `cluster_cap[c]` (c <= TC_MAX_CLUSTER), when
+// given, is how many clusters of c CTAs of this kernel the device holds at once; a plan uses cluster reduction only
+// if all of its clusters fit at once (one wave), so no cluster waits for another to finish.
+inline TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int split_k, int sms, const int* cluster_cap = nullptr) {
   TcPlan p;
   p.BT = tc_pick_bt(M);
   p.m_tiles = (int)((M + p.BT - 1) / p.BT);
@@ -168,9 +183,24 @@ inline TcPlan tc_plan(int64_t M, int64_t N, int64_t K, int split_k, int sms) {
   p.stages = (int)std::min<size_t>(8, (TC_SMEM_BUDGET - overhead) / stage);
   p.smem = (size_t)p.stages * stage + overhead;
   const bool aligned = (groups <= p.n_tiles) && (p.n_tiles % groups == 0);  // every group covers whole n-tiles
+  // cluster reduction: every n-tile cut into ks >= 2 K parts (one per group), one segment per CTA (one m-tile chunk)
+  p.ks = 0;
+  p.cs = 1;
+  if (cluster_cap && !aligned && groups % p.n_tiles == 0 && p.chunks == 1) {
+    const int64_t ks = groups / p.n_tiles;
+    const int64_t cs = ks * p.gs;
+    // the partial tile ([BT][128] int64) is written over the pipeline stages, so it must fit in them
+    const size_t red = (size_t)p.BT * 128 * 8, stages_bytes = (size_t)std::min<size_t>(
+        8, (TC_SMEM_BUDGET - (1024 + 256 + TC_RED_STAGING + TC_TOK_WORDS)) / tc_stage_bytes(p.BT)) * tc_stage_bytes(p.BT);
+    if (ks >= 2 && ks <= p.KI && cs <= TC_MAX_CLUSTER && (int64_t)cluster_cap[cs] * cs >= (int64_t)p.G &&
+        red <= stages_bytes) {
+      p.ks = (int)ks;
+      p.cs = (int)cs;
+    }
+  }
   const int64_t slots = (groups - 1) * (int64_t)p.m_tiles;  // one per (group boundary, m-tile)
   p.cnt_bytes = (size_t)((slots * 4 + 255) / 256 * 256);
-  p.ws_bytes = (aligned || slots == 0) ? 0 : p.cnt_bytes + (size_t)slots * p.BT * 128 * 8;
+  p.ws_bytes = (aligned || slots == 0 || p.cs > 1) ? 0 : p.cnt_bytes + (size_t)slots * p.BT * 128 * 8;
   // (slot layout [4 lane quarters][BT tokens][32 rows] per 128 rows: each epilogue warp reduces contiguous 1 KB)
   return p;
 }
@@ -185,6 +215,7 @@ inline void tc_plan_args(const TcPlan& p, TcArgs& a) {
   a.groups = p.groups;
   a.chunks = p.chunks;
   a.stages = p.stages;
+  a.ks = p.cs > 1 ? p.ks : 0;
 }
 
 }  // namespace ex

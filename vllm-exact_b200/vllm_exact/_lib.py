@@ -13,6 +13,7 @@ EX_OK, EX_ERR_ARG, EX_ERR_ALIGN, EX_ERR_WORKSPACE, EX_ERR_DTYPE, EX_ERR_UNSUPPOR
 EX_DTYPE_F32, EX_DTYPE_BF16, EX_DTYPE_F16 = 0, 1, 2
 EX_IPC_HANDLE_BYTES = 64
 EX_ALGO_AUTO, EX_ALGO_SIMT, EX_ALGO_TC_I8 = 0, 1, 2
+EX_LINEAR_STATIC_WEIGHTS = 0x100  # flag OR-ed into algo (vllm_exact_b200.h)
 
 c_i64, c_i32, c_vp, c_sz, c_f32 = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_float
 

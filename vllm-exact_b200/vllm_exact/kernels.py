@@ -18,6 +18,7 @@ used to check this module lives in the repository's oracle/ directory (test infr
 from __future__ import annotations
 
 import threading
+import weakref
 
 import torch
 
@@ -25,8 +26,8 @@ from . import _lib
 from ._lib import EX_ALGO_AUTO, EX_ALGO_SIMT, EX_ALGO_TC_I8, check, lib
 
 __all__ = ["digitize", "digitize_weight", "exact_linear", "exact_linear_partial_i64", "exact_epilogue",
-           "autotune_exact", "EXACT_CFGS", "reserve_workspace", "reset_workspaces", "EX_ALGO_AUTO", "EX_ALGO_SIMT",
-           "EX_ALGO_TC_I8"]
+           "autotune_exact", "EXACT_CFGS", "reserve_workspace", "reset_workspaces", "mark_static", "is_static",
+           "EX_ALGO_AUTO", "EX_ALGO_SIMT", "EX_ALGO_TC_I8"]
 
 _DT = {torch.float32: _lib.EX_DTYPE_F32, torch.bfloat16: _lib.EX_DTYPE_BF16, torch.float16: _lib.EX_DTYPE_F16}
 _LD_ALIGN = 16  # digit rows are padded to 16 bytes so the tensor-core kernels can TMA them
@@ -89,6 +90,49 @@ def reserve_workspace(nbytes: int, device=None, stream=None) -> None:
 
 
 # ------------------------------------------------------------------------------------------------------------------
+# static weight digits: may be read before the kernels ahead of a GEMM on the stream have finished
+# ------------------------------------------------------------------------------------------------------------------
+_STATIC = {}  # data_ptr -> number of live marked tensors starting there
+_STATIC_LOCK = threading.Lock()
+
+
+def _unmark(ptr: int) -> None:
+    with _STATIC_LOCK:
+        n = _STATIC.get(ptr, 0) - 1
+        if n > 0:
+            _STATIC[ptr] = n
+        else:
+            _STATIC.pop(ptr, None)
+
+
+def mark_static(*tensors: torch.Tensor) -> None:
+    """Declare weight digit tensors static. Synchronizes their devices first, so every kernel that wrote them has
+    finished; from then on exact_linear lets the tensor-core GEMM start loading them before the kernels ahead of it on
+    the stream have finished (EX_LINEAR_STATIC_WEIGHTS), which takes the weight stream's start off the critical path
+    of back-to-back layers. A tensor stays marked while it is alive, and must not be written afterwards (writing
+    through digitize(out=...) removes the mark). digitize_weight marks its results."""
+    for dev in {t.device for t in tensors if t.is_cuda}:
+        torch.cuda.synchronize(dev)
+    for t in tensors:
+        ptr = t.data_ptr()
+        with _STATIC_LOCK:
+            _STATIC[ptr] = _STATIC.get(ptr, 0) + 1
+        weakref.finalize(t, _unmark, ptr)
+
+
+def is_static(*tensors: torch.Tensor) -> bool:
+    """True when every tensor starts where a live tensor marked by mark_static starts."""
+    with _STATIC_LOCK:
+        return all(t.data_ptr() in _STATIC for t in tensors)
+
+
+def _clear_marks(*tensors: torch.Tensor) -> None:
+    with _STATIC_LOCK:
+        for t in tensors:
+            _STATIC.pop(t.data_ptr(), None)
+
+
+# ------------------------------------------------------------------------------------------------------------------
 # digitization
 # ------------------------------------------------------------------------------------------------------------------
 def _alloc_digits(R: int, K: int, dev):
@@ -113,6 +157,8 @@ def digitize(x: torch.Tensor, F: int, out=None):
     R, K = x.shape
     if out is None:
         out = _alloc_digits(R, K, x.device)
+    elif _STATIC:
+        _clear_marks(*out)
     h, l, cs, sh = out
     if h.stride(1) != 1 or l.stride(1) != 1 or h.stride(0) != l.stride(0):
         raise ValueError("digit buffers must be row-major with equal leading dimensions")
@@ -124,13 +170,15 @@ def digitize(x: torch.Tensor, F: int, out=None):
 
 
 def digitize_weight(w: torch.Tensor, F: int, rows_per_block: int = 32768):
-    """Digitize a weight matrix once at load time (reference plugin.py:72-79), in row blocks."""
+    """Digitize a weight matrix once at load time (reference plugin.py:72-79), in row blocks. The digits are marked
+    static (mark_static, which synchronizes the device)."""
     _need_cuda(w)
     N, K = w.shape
     out = _alloc_digits(N, K, w.device)
     for i in range(0, N, rows_per_block):
         j = min(N, i + rows_per_block)
         digitize(w[i:j], F, out=tuple(t[i:j] for t in out))
+    mark_static(*out)
     return out
 
 
@@ -227,6 +275,8 @@ def exact_linear(xd, wd, F: int, trunc: bool = False, out: torch.Tensor | None =
     with torch.cuda.device(xh.device):
         nbytes = L.ex_linear_workspace_bytes(M, N, K, sk, algo)
         ws = _workspace(xh.device, nbytes)
+        if _STATIC and is_static(wh, wl):
+            algo |= _lib.EX_LINEAR_STATIC_WEIGHTS
         check("ex_linear", L.ex_linear(xh.data_ptr(), xl.data_ptr(), xh.stride(0), cx.data_ptr(), sx.data_ptr(),
                                        wh.data_ptr(), wl.data_ptr(), wh.stride(0), cw.data_ptr(), sw.data_ptr(), M, N,
                                        K, F, int(bool(trunc)), out.data_ptr(), _DT[out.dtype], out.stride(0),
@@ -251,6 +301,8 @@ def exact_linear_partial_i64(xd, wd, F: int, trunc: bool = False, out: torch.Ten
     with torch.cuda.device(xh.device):
         nbytes = L.ex_linear_workspace_bytes(M, N, K, sk, algo)
         ws = _workspace(xh.device, nbytes)
+        if _STATIC and is_static(wh, wl):
+            algo |= _lib.EX_LINEAR_STATIC_WEIGHTS
         check("ex_linear_partial_i64",
               L.ex_linear_partial_i64(xh.data_ptr(), xl.data_ptr(), xh.stride(0), cx.data_ptr(), wh.data_ptr(),
                                       wl.data_ptr(), wh.stride(0), cw.data_ptr(), M, N, K, F, int(bool(trunc)),

@@ -88,19 +88,23 @@ def digitize_weight_row_sharded(w: torch.Tensor, F: int, group=None, ops=CudaOps
         wb = w[i:i + rows_per_block]
         parts.append(ops.digitize_given(wb, F, global_row_absmax(wb, group, ops)))
     if len(parts) == 1:
-        return parts[0]
-    # concatenate, keeping the 16-byte-aligned leading dimension of the digit rows
-    N, Kd = w.shape
-    h, l, cs, sh = K._alloc_digits(N, Kd, w.device) if w.is_cuda else [None] * 4
-    if h is None:
-        return tuple(torch.cat([p[j] for p in parts]) for j in range(4))
-    r = 0
-    for p in parts:
-        n = p[0].shape[0]
-        for dst, src in zip((h, l, cs, sh), p):
-            dst[r:r + n].copy_(src)
-        r += n
-    return h, l, cs, sh
+        out = parts[0]
+    else:
+        # concatenate, keeping the 16-byte-aligned leading dimension of the digit rows
+        N, Kd = w.shape
+        h, l, cs, sh = K._alloc_digits(N, Kd, w.device) if w.is_cuda else [None] * 4
+        if h is None:
+            return tuple(torch.cat([p[j] for p in parts]) for j in range(4))
+        r = 0
+        for p in parts:
+            n = p[0].shape[0]
+            for dst, src in zip((h, l, cs, sh), p):
+                dst[r:r + n].copy_(src)
+            r += n
+        out = (h, l, cs, sh)
+    if w.is_cuda:
+        K.mark_static(*out)  # load time: later GEMMs may start streaming these digits early
+    return out
 
 
 def row_parallel_linear(x: torch.Tensor, wh, wl, cw, sw, F: int, trunc: bool, group=None, ops=CudaOps,
