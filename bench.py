@@ -214,6 +214,7 @@ def run_ours(args):
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+        return run_tp(args, dev, rank, world, local)
     hbm, bf16_burst, bf16_sust, peak_kind = peaks()
 
     # ---------------- workload: weights resident in HBM, activations per (M, shape)
@@ -343,6 +344,249 @@ def run_ours(args):
         print(json.dumps(result), flush=True)
 
 
+# ------------------------------------------------------------------------------------------------------------------
+# tensor-parallel arm (--gpus N > 1): the same decode sweep, every layer sharded over the N ranks
+# ------------------------------------------------------------------------------------------------------------------
+ROW_PARALLEL = ("o_proj", "down")  # K-sharded (row-parallel); the others are N-sharded (column-parallel)
+
+
+def tp_shards(rank, world, dev):
+    """This rank's shard of every headline weight matrix, cut from the full digits of the 1-GPU run (same seeds):
+    column-parallel layers keep rows [r N/p, (r+1) N/p) of the full-K digits; row-parallel layers keep columns
+    [r K/p, (r+1) K/p) of digits made with whole-row scales, which is exactly what digitize_weight_row_sharded
+    produces (row maxima all-reduced with MAX before digitizing; F = 14 has no row sums)."""
+    from vllm_exact import kernels as KK
+    W = {}
+    for i, (name, K, N) in enumerate(SHAPES):
+        full = make_weight_digits(K, N, 1000 + i, dev)
+        if name in ROW_PARALLEL:
+            ks = K // world
+            c = slice(rank * ks, (rank + 1) * ks)
+            shard = (full[0][:, c].contiguous(), full[1][:, c].contiguous(), full[2].clone(), full[3].clone())
+        else:
+            ns = N // world
+            r = slice(rank * ns, (rank + 1) * ns)
+            shard = tuple(t[r].contiguous() for t in full)
+        KK.mark_static(*shard)
+        W[name] = shard
+        del full
+    return W
+
+
+def run_tp(args, dev, rank, world, local):
+    """--gpus N > 1: the headline decode sweep as an N-way tensor-parallel model would run it. qkv, gate_up and
+    lm_head are column-parallel (each rank: full activations, N/p weight rows, its slice of the outputs; no
+    collective); o_proj and down are row-parallel through parallel.PeerRowParallel (row maxima of the K slice
+    exchanged over peer memory and the slice digitized with the whole-row maxima -> int64 partial GEMM ->
+    reduce-scatter + epilogue + all-gather over peer memory; every rank holds the full output). The same step with
+    NCCL all-reduces for both exchanges (parallel.row_parallel_linear) is timed beside it. value =
+    the algorithmic bytes of the whole 15-GEMM step (the same bytes as on one GPU, now spread over N GPUs) / the
+    step's device time, max over ranks: total work is fixed, so scaling is strong. Every output row sample is checked
+    against the CPU oracle (row-parallel outputs against the unsharded weights), so the line also shows that N GPUs
+    give the 1-GPU bits."""
+    import torch
+    import torch.distributed as dist
+    from vllm_exact import kernels as KK, parallel as P
+    g = dist.group.WORLD
+    hbm, _, _, peak_kind = peaks()
+    W = tp_shards(rank, world, dev)
+    X = {(M, name): make_activation(M, K, 17 * M + i, dev) for M in DECODE_M for i, (name, K, N) in enumerate(SHAPES)}
+    XS = {}  # row-parallel inputs: this rank's K slice
+    for (M, name), x in X.items():
+        if name in ROW_PARALLEL:
+            ks = x.shape[1] // world
+            XS[(M, name)] = x[:, rank * ks:(rank + 1) * ks].contiguous()
+    order = [(M, name, K, N) for M in DECODE_M for name, K, N in SHAPES]
+    step_bytes = sum(gemm_bytes(M, K, N) for M, name, K, N in order)
+    Y = {(M, name): torch.empty(M, N if name in ROW_PARALLEL else N // world, device=dev, dtype=torch.bfloat16)
+         for M, name, K, N in order}
+    stream = torch.cuda.Stream(dev)
+
+    def ws_need(M, name, K, N):
+        return KK.lib().ex_linear_workspace_bytes(M, N, K // world, 0, 0) if name in ROW_PARALLEL else \
+            KK.lib().ex_linear_workspace_bytes(M, N // world, K, 0, 0)
+    KK.reserve_workspace(max(ws_need(*o) for o in order), dev, stream=stream)
+
+    peer = P.PeerRowParallel(max(DECODE_M), max(N for name, K, N in SHAPES if name in ROW_PARALLEL), group=g)
+
+    def layer(M, name, path="peer"):
+        if name not in ROW_PARALLEL:
+            KK.exact_linear(KK.digitize(X[(M, name)], 14), W[name], 14, True, out=Y[(M, name)])
+        elif path == "peer":
+            peer.linear(XS[(M, name)], *W[name], 14, True, out=Y[(M, name)])
+        else:
+            P.row_parallel_linear(XS[(M, name)], *W[name], 14, True, group=g, out=Y[(M, name)])
+
+    def step(path="peer"):
+        for M, name, K, N in order:
+            layer(M, name, path)
+
+    def graph_of(fn, warm=2):
+        with torch.cuda.stream(stream):
+            for _ in range(warm):
+                fn()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=stream):
+            fn()
+        return gr
+
+    def timed(gr, reps):
+        for _ in range(2):
+            gr.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            a.record()
+            for _ in range(reps):
+                gr.replay()
+            b.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b) / reps], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t)
+
+    ms_nccl = timed(graph_of(lambda: step("nccl")), args.steps)  # the same step with NCCL for both exchanges
+    gS = graph_of(step, warm=args.warmup)
+    for _ in range(args.warmup):
+        gS.replay()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        clk.wait_first_sample()
+        dist.barrier()
+        torch.cuda.synchronize()
+        c0 = clk.mark()
+        with torch.cuda.stream(stream):
+            t0.record()
+            for _ in range(args.steps):
+                gS.replay()
+            t1.record()
+        torch.cuda.synchronize()
+        c1 = clk.mark()
+    dist.barrier()
+    tt = torch.tensor([t0.elapsed_time(t1)], device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms_per_step = float(tt) / args.steps
+    value = step_bytes / (ms_per_step * 1e-3) / 1e12
+
+    # the GEMM kernels alone (digits computed once; row-parallel layers write their int64 partials), this rank
+    XD = {key: KK.digitize(x, 14) for key, x in X.items() if key[1] not in ROW_PARALLEL}
+    for key, x in XS.items():
+        XD[key] = P.CudaOps.digitize_given(x, 14, P.global_row_absmax(x, g))
+    PART = {(M, name): torch.empty(M, N, device=dev, dtype=torch.int64) for M, name, K, N in order
+            if name in ROW_PARALLEL}
+
+    def gemms():
+        for M, name, K, N in order:
+            if name in ROW_PARALLEL:
+                KK.exact_linear_partial_i64(XD[(M, name)], W[name], 14, True, out=PART[(M, name)])
+            else:
+                KK.exact_linear(XD[(M, name)], W[name], 14, True, out=Y[(M, name)])
+    gemm_ms = timed(graph_of(gemms), args.steps)
+    rank_bytes = sum(2 * (N // world if name not in ROW_PARALLEL else N) * (K if name not in ROW_PARALLEL else
+                                                                            K // world) for M, name, K, N in order)
+    # the step re-run after the GEMM-only graph, so Y holds the step's outputs for the bit check
+    gS.replay()
+    torch.cuda.synchronize()
+
+    # per layer: 10 calls back to back in one graph (us per call, max over ranks), and the two collectives alone
+    per_layer, coll = {}, {}
+    for M, name, K, N in order:
+        row = {}
+        for path in (("peer", "nccl") if name in ROW_PARALLEL else ("peer",)):
+            gl = graph_of(lambda: [layer(M, name, path) for _ in range(10)])
+            row[path] = round(timed(gl, 5) * 100, 2)
+            del gl
+        per_layer[f"{name}/M{M}"] = row if name in ROW_PARALLEL else row["peer"]
+    for M in DECODE_M:
+        amax = torch.ones(M, device=dev)
+        tot = torch.zeros(M, 4096, dtype=torch.int64, device=dev)
+        gm = graph_of(lambda: [dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=g) for _ in range(10)])
+        gsum = graph_of(lambda: [dist.all_reduce(tot, op=dist.ReduceOp.SUM, group=g) for _ in range(10)])
+        coll[f"M{M}"] = {"max_f32_us": round(timed(gm, 5) * 100, 2),
+                         "sum_i64_M_x_4096_us": round(timed(gsum, 5) * 100, 2)}
+        del gm, gsum
+
+    # end to end through the public API with host buffers: inputs copied in from pinned host memory and outputs
+    # copied back into pinned host memory inside the timed graph, on every rank
+    H = {k: (XS[k] if k[1] in ROW_PARALLEL else X[k]).cpu().pin_memory() for k in X}
+    O = {k: torch.empty(Y[k].shape, dtype=torch.bfloat16).pin_memory() for k in Y}
+    DX = {k: torch.empty_like(v, device=dev) for k, v in H.items()}
+
+    def e2e_step():
+        for M, name, K, N in order:
+            k = (M, name)
+            DX[k].copy_(H[k], non_blocking=True)
+            if name in ROW_PARALLEL:
+                peer.linear(DX[k], *W[name], 14, True, out=Y[k])
+            else:
+                KK.exact_linear(KK.digitize(DX[k], 14), W[name], 14, True, out=Y[k])
+            O[k].copy_(Y[k], non_blocking=True)
+    e2e_ms = timed(graph_of(e2e_step), max(3, args.steps // 4))
+    h2d = world * sum(v.numel() * 2 for v in H.values())
+    d2h = world * sum(v.numel() * 2 for v in O.values())
+
+    # bit check against the CPU oracle on a row sample (rank by rank; row-parallel layers against the full weights)
+    gS.replay()
+    torch.cuda.synchronize()
+    check = {"ok": True, "elements": 0, "mismatches": 0, "first_mismatch": None}
+    if not args.quick:
+        Wc, oc = {}, []
+        for i, (name, K, N) in enumerate(SHAPES):
+            if name in ROW_PARALLEL:
+                Wc[name] = make_weight_digits(K, N, 1000 + i, dev)
+                oc += [(M, name, K, N) for M in DECODE_M]
+            else:
+                Wc[name] = W[name]
+                oc += [(M, name, K, N // world) for M in DECODE_M]
+        r = bitwise_check(Wc, X, Y, oc)
+        del Wc
+        agg = torch.tensor([r["elements"], r["mismatches"]], dtype=torch.int64, device=dev)
+        dist.all_reduce(agg, op=dist.ReduceOp.SUM)
+        check = {"ok": int(agg[1]) == 0, "elements": int(agg[0]), "mismatches": int(agg[1]),
+                 "first_mismatch": r["first_mismatch"],
+                 "sample": "every rank: rows {0, M-1} of each of its 15 layer outputs x all its output columns vs the "
+                           "CPU oracle of the unsharded layer (bf16 bits)"}
+    launches = sum(3 if name in ROW_PARALLEL else 2 for M, name, K, N in order)
+    result = {
+        "metric": METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8 digits (exact int32/int64), bf16 in/out", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "parallelism": f"tp{world}",
+                   "sharding": "qkv, gate_up, lm_head column-parallel (N/p weight rows per rank, outputs stay "
+                               "sharded); o_proj, down row-parallel (K/p per rank, full output on every rank): row "
+                               "maxima exchanged and the slice digitized in one peer-memory kernel, partial int64 GEMM, "
+                               "reduce-scatter + epilogue + all-gather in one peer-memory kernel (NVLink loads and "
+                               "stores, no NCCL on the data path)",
+                   "ms_per_step_nccl": round(ms_nccl, 4),
+                   "l2": "inputs larger than L2: each rank rotates its 1.63/p GB of weight digits",
+                   "per_step_bytes": step_bytes, "timing": "CUDA graph of one step (NCCL collectives captured), "
+                   "replayed --steps times between two events, max over ranks"},
+        "gpu_launches": launches * args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(rank_bytes / (gemm_ms * 1e-3) / 1e9, 1), "peak": hbm,
+                     "unit": "GB/s", "frac": round(rank_bytes / (gemm_ms * 1e-3) / 1e9 / hbm, 4), "traffic": None,
+                     "peak_kind": peak_kind,
+                     "kernel": "k_exact_tc_i8 on one rank: its 15 GEMM launches of the step back to back in one "
+                               "CUDA graph (weight-digit bytes of its shards / time, max over ranks)"},
+        "clocks": clk.summary(c0, c1),
+        "e2e": {"value": round(step_bytes / (e2e_ms * 1e-3) / 1e12, 4), "unit": "TB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4),
+                "api": "kernels.exact_linear / parallel.row_parallel_linear per rank, pinned host in and out inside "
+                       "one CUDA graph per step, max over ranks"},
+        "per_layer_us": per_layer, "collectives_us": coll,
+        "bitwise": check, "bitwise_ok": check["ok"],
+    }
+    del gS
+    torch.cuda.synchronize()
+    dist.barrier()
+    peer.close()
+    dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
 def _graph_time(fns, reps, stream, warm=2):
     """Capture `fns` (a list of launch callables) into one CUDA graph with external timing events around each, replay
     it `reps` times, and return (ms per replay, [median ms of each fn])."""
@@ -399,30 +643,38 @@ def int8_peak(dev, n=8192, reps=10):
 
 
 def tensor_sweep(dev, W, peak_bf16, quick):
-    """M in {256, 4096}: one graph per M with the five shapes in sequence (weights rotate through L2). Executed
-    digit-product ops (6 M N K) against the measured bf16 dense peak and against the INT8 dense peak measured here
-    (the kernel runs INT8 MMAs, which B200 executes at twice the bf16 rate, so frac_i8_peak is its roofline)."""
+    """M in {256, 4096}, the tensor-bound part of configs[1]: each (shape, M) timed as a chain of GEMMs back to back in
+    one CUDA graph (digits computed beforehand; weights rotating over copies worth >= 3 x L2, as in decode_layers).
+    Executed digit-product ops (6 M N K) against the INT8 dense peak measured here (the kernel runs INT8 MMAs, which
+    B200 executes at twice the bf16 rate, so frac_i8_peak is its roofline) and, for reference, the measured bf16 dense
+    peak."""
     import torch
     from vllm_exact import kernels as KK
     stream = torch.cuda.Stream(dev)
     peak_i8 = int8_peak(dev)
     out = {"int8_peak_TOPs": round(peak_i8, 1)}
-    for M in TENSOR_M:
-        if quick and M > 256:
-            continue
-        xs = {name: KK.digitize(make_activation(M, K, 7 * M + i, dev), 14) for i, (name, K, N) in enumerate(SHAPES)}
-        ys = {name: torch.empty(M, N, device=dev, dtype=torch.bfloat16) for name, K, N in SHAPES}
-        KK.reserve_workspace(max(KK.lib().ex_linear_workspace_bytes(M, N, K, 0, 0) for _, K, N in SHAPES), dev,
-                             stream=stream)
-        fns = [(lambda name=name: KK.exact_linear(xs[name], W[name], 14, True, out=ys[name])) for name, K, N in SHAPES]
-        _, per = _graph_time(fns, 3 if M > 256 else 10, stream)
-        for (name, K, N), ms in zip(SHAPES, per):
+    for i, (name, K, N) in enumerate(SHAPES):
+        C = max(1, -(-3 * L2_BYTES // (2 * N * K)))
+        Wc = [W[name]] + [tuple(t.clone() for t in W[name]) for _ in range(C - 1)]
+        for w in Wc[1:]:
+            KK.mark_static(*w)
+        for M in TENSOR_M:
+            if quick and M > 256:
+                continue
+            xd = KK.digitize(make_activation(M, K, 7 * M + i, dev), 14)
+            y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            KK.reserve_workspace(KK.lib().ex_linear_workspace_bytes(M, N, K, 0, 0), dev, stream=stream)
+            R = C * max(1, -(-(4 if M > 256 else 8) // C))
+            us = _chain_time(lambda r: KK.exact_linear(xd, Wc[r % C], 14, True, out=y), R, stream,
+                             reps=2 if M > 256 else 5)
             fl = 6.0 * M * N * K
-            out[f"{name}/M{M}"] = {"us": round(ms * 1e3, 1), "TOPs_executed": round(fl / ms / 1e9, 1),
-                                   "frac_i8_peak": round(fl / ms / 1e9 / peak_i8, 3),
-                                   "frac_bf16_peak": round(fl / ms / 1e9 / peak_bf16, 3),
-                                   "TOPs_useful": round(fl / 3 / ms / 1e9, 1)}
-        del xs, ys
+            out[f"{name}/M{M}"] = {"us": round(us, 1), "TOPs_executed": round(fl / us / 1e6, 1),
+                                   "frac_i8_peak": round(fl / us / 1e6 / peak_i8, 3),
+                                   "frac_bf16_peak": round(fl / us / 1e6 / peak_bf16, 3),
+                                   "TOPs_useful": round(fl / 3 / us / 1e6, 1)}
+            del xd, y
+        del Wc
+        torch.cuda.empty_cache()
     return out
 
 
@@ -801,14 +1053,14 @@ def run_reference(args):
 ENGINE_MAX_LEN = 21504  # prompts up to 1.25 x 16K plus 321 generated tokens
 
 
-def _engine_model_dir():
+def _engine_model_dir(layers=32):
     """config.json of BASELINE configs[4]'s model: the qwen3_5 text architecture with hidden 4096, 32 layers (24
     Gated-DeltaNet + 8 full attention, GQA 32q/8kv x 128), SwiGLU 12288, vocab 151936; GDN heads give in_proj_qkvz
     N = 12288 and in_proj_ba N = 64 (the reference's tuned shapes). Weights are vLLM's dummy (random) init."""
     import json
     import tempfile
     cfg = {"architectures": ["HybridQwen35ForCausalLM"], "model_type": "qwen3_5_text", "hidden_size": 4096,
-           "intermediate_size": 12288, "num_hidden_layers": 32, "num_attention_heads": 32, "num_key_value_heads": 8,
+           "intermediate_size": 12288, "num_hidden_layers": layers, "num_attention_heads": 32, "num_key_value_heads": 8,
            "head_dim": 128, "vocab_size": 151936, "linear_num_key_heads": 16, "linear_num_value_heads": 32,
            "linear_key_head_dim": 128, "linear_value_head_dim": 128, "linear_conv_kernel_dim": 4,
            "full_attention_interval": 4, "max_position_embeddings": 32768, "rms_norm_eps": 1e-6,
@@ -822,8 +1074,11 @@ def _engine_model_dir():
 
 def _register_engine_model():
     """vLLM 0.22 ships the text-only Qwen3.5 model class without the hybrid (GDN state) interface that only its
-    vision-language twin declares; give it that interface (the twin's own state-shape hooks) and register it."""
+    vision-language twin declares; give it that interface (the twin's own state-shape hooks) and register it. Runs in
+    every vLLM process (tensor-parallel workers too) through vllm_exact.vllm_plugin's extra hooks; idempotent."""
     from vllm import ModelRegistry
+    if "HybridQwen35ForCausalLM" in ModelRegistry.get_supported_archs():
+        return
     from vllm.model_executor.models.interfaces import IsHybrid
     from vllm.model_executor.models.qwen3_5 import Qwen3_5ForCausalLM, Qwen3_5ForConditionalGeneration as VL
 
@@ -843,23 +1098,31 @@ def engine_case(args):
     1,024-token prompts, alone (A), interleaved into a batch of 64 (B), alone again (C), 256 generated tokens, greedy
     and temperature 1.0 (top-k 20, top-p 0.95, per-request seeds), tokens and logprobs compared bitwise; speed =
     (t(321 new tokens) - t(65 new tokens)) / 256 with the minimum of two runs each, at (256, 1K), (64, 8K), (16, 16K),
-    prompt lengths uniform in [0.75, 1.25] x ctx. Prints one JSON line. One arm per process."""
+    prompt lengths uniform in [0.75, 1.25] x ctx. Prints one JSON line. One arm per process. Options after the arm:
+    `tp=N` (tensor-parallel size), `layers=L` (default 32), `inv` (invariance only, no speed runs)."""
     import random
     import time
-    arm = args.case.split(":")[1] if ":" in args.case else "exact"
+    parts = args.case.split(":")
+    arm = parts[1] if len(parts) > 1 else "exact"
+    opts = dict(o.split("=") if "=" in o else (o, "1") for o in parts[2:])
+    tp, layers, inv_only = int(opts.get("tp", 1)), int(opts.get("layers", 32)), opts.get("inv") == "1"
     kw = {}
     if arm == "exact":
         import vllm_exact
         kw = vllm_exact.enable(max_model_len=ENGINE_MAX_LEN)
+        # tensor-parallel workers register the model class through the package's vLLM plugin hook
+        os.environ[vllm_exact.EXTRA_PLUGINS_ENV] = "bench:_register_engine_model"
     else:
         os.environ["VLLM_ENABLE_V1_MULTIPROCESSING"] = "0"
         kw = {"enable_prefix_caching": False}
     _register_engine_model()
     from vllm import LLM, SamplingParams
     t0 = time.time()
-    llm = LLM(model=_engine_model_dir(), load_format="dummy", skip_tokenizer_init=True, dtype="bfloat16",
-              max_model_len=ENGINE_MAX_LEN, gpu_memory_utilization=0.85, max_num_seqs=256, seed=0, **kw)
-    res = {"arm": arm, "startup_s": round(time.time() - t0, 1), "invariance": {}, "speed": {}}
+    llm = LLM(model=_engine_model_dir(layers), load_format="dummy", skip_tokenizer_init=True, dtype="bfloat16",
+              max_model_len=ENGINE_MAX_LEN, gpu_memory_utilization=0.85, max_num_seqs=256, seed=0,
+              tensor_parallel_size=tp, **kw)
+    res = {"arm": arm, "tp": tp, "layers": layers, "startup_s": round(time.time() - t0, 1), "invariance": {},
+           "speed": {}}
 
     def prompts_of(n, lo, hi, seed):
         rng = random.Random(seed)
@@ -892,7 +1155,7 @@ def engine_case(args):
             res["invariance"][f"T{temp}"] = {"A_vs_B_tokens_logprobs": "%d/16, %d/16" % same(A, B),
                                              "A_vs_C_tokens_logprobs": "%d/16, %d/16" % same(A, C)}
             print(json.dumps({"partial": res}), file=sys.stderr, flush=True)
-    for n, ctx in (STEP_CONFIGS[:1] if args.quick else STEP_CONFIGS):
+    for n, ctx in ([] if inv_only else STEP_CONFIGS[:1] if args.quick else STEP_CONFIGS):
         prompts = [{"prompt_token_ids": p} for p in prompts_of(n, int(0.75 * ctx), int(1.25 * ctx), n * 7 + ctx)]
 
         def gen(k):
@@ -910,10 +1173,10 @@ def engine_case(args):
 
 def tp_case(args):
     """Row-parallel (K-sharded) exact layers on the torchrun group: time per layer call of the NCCL path (int64 SUM
-    all-reduce + epilogue kernel) and of the fused peer-memory path (PeerEpilogue: one kernel reads the peers'
-    partials over NVLink and applies the epilogue), both captured in CUDA graphs (20 calls per graph), device time,
-    max over ranks. Both paths include the row-max all-reduce, the digitizer and the partial GEMM. Prints one JSON
-    line on rank 0. Launch: torchrun --nproc-per-node N bench.py --case tp."""
+    all-reduce + epilogue kernel) and of the peer-memory path (PeerRowParallel: the row-maxima exchange + digitize and
+    the reduce-scatter + epilogue + all-gather as kernels over NVLink), both captured in CUDA graphs (20 calls per
+    graph), device time, max over ranks. Both paths include the digitizer and the partial GEMM. Prints one JSON line
+    on rank 0. Launch: torchrun --nproc-per-node N bench.py --case tp."""
     import datetime
     import torch
     import torch.distributed as dist
@@ -923,7 +1186,7 @@ def tp_case(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
-    peer = P.PeerEpilogue(64, 4096)
+    peer = P.PeerRowParallel(64, 4096)
     res = {}
     for name, Kd, N in (("o_proj", 4096, 4096), ("down", 12288, 4096)):
         ks = Kd // world

@@ -3,6 +3,7 @@ vLLM is imported (reference __init__.py:44-47). Prints one JSON object with the 
 
     python tests/surface_driver.py enable      # CPU: enable() kwargs, registration, patch, guards
     python tests/surface_driver.py plugin      # GPU: exact_int8 linear / lm_head methods and the FA decode patch
+    python tests/surface_driver.py worker      # CPU: the vLLM general-plugin entry point in a process without enable()
 """
 import json
 import os
@@ -36,6 +37,32 @@ def check_enable():
         out["second_call"] = str(e)
     import torch
     out["custom_op"] = str(torch.ops.exactmm.linear)
+    # the vLLM general-plugin entry point is discoverable, and running it again in this process changes nothing
+    from importlib.metadata import entry_points
+    out["entry_points"] = [e.value for e in entry_points(group="vllm.general_plugins") if "vllm_exact" in e.value]
+    before = fa.FlashAttentionImpl.forward
+    vllm_exact.vllm_plugin()
+    out["plugin_idempotent"] = fa.FlashAttentionImpl.forward is before
+    out["settings_env"] = json.loads(os.environ[vllm_exact.SETTINGS_ENV])
+    return out
+
+
+def check_worker():
+    """A process that never ran enable(), as a vLLM tensor-parallel worker: vLLM calls the general-plugin entry point,
+    which applies the settings enable() recorded in the environment."""
+    import vllm  # noqa: F401  (a worker has vLLM imported before plugins load)
+    import vllm_exact
+    vllm_exact.vllm_plugin()
+    out = {}
+    from vllm.model_executor.layers.quantization import get_quantization_config
+    out["quant_config"] = get_quantization_config("exact_int8").__module__
+    from vllm.v1.attention.backends import flash_attn as fa
+    out["fa_forward_file"] = Path(fa.FlashAttentionImpl.forward.__code__.co_filename).name
+    from vllm.v1.attention.backends.gdn_attn import GDNAttentionBackend
+    out["gdn_invariant"] = bool(GDNAttentionBackend.supports_batch_invariance())
+    from vllm_exact import ops, paged_attn, plugin
+    out["max_len"] = paged_attn.MAX_LEN
+    out["plugin"] = [plugin.F, plugin.TRUNC, plugin.LMHEAD, ops.F]
     return out
 
 
@@ -118,5 +145,5 @@ def check_plugin():
 
 if __name__ == "__main__":
     mode = sys.argv[1]
-    res = check_enable() if mode == "enable" else check_plugin()
+    res = {"enable": check_enable, "plugin": check_plugin, "worker": check_worker}[mode]()
     print("SURFACE_JSON " + json.dumps(res), flush=True)

@@ -74,17 +74,32 @@ def test_argument_validation_without_gpu(L):
     assert L.ex_paged_decode_leading(*lead(ctypes.c_void_p(18))) == X.EX_ERR_ALIGN
     assert L.ex_paged_decode_leading(*lead(ctypes.c_void_p(16))) == X.EX_ERR_WORKSPACE
     assert L.ex_paged_decode_leading(*lead(None)) == X.EX_ERR_WORKSPACE  # NULL: plain decode of all n requests
-    # fused tensor-parallel epilogue: rank outside [0, world), world < 1, bad dtype, leading dimensions < N, NULL
-    ar = lambda rank, world, od, ldt, ldo, M=4, N=8, parts=p: (parts, ldt, p, p, rank, world, p, p, M, N, p, od, ldo,
-                                                              None)
+    # peer-memory all-reduce + epilogue: rank outside [0, world), world < 1 or > 16, bad dtype, leading dimensions
+    # < N, NULL buffers, odd N / leading dimensions (column pairs)
+    ar = lambda rank, world, od, ldt, ldo, M=4, N=8, parts=p, outs=p: (parts, ldt, outs, p, p, rank, world, p, p, M,
+                                                                      N, p, od, ldo, None)
     assert L.ex_allreduce_epilogue_i64(*ar(2, 2, 1, 8, 8)) == X.EX_ERR_ARG
     assert L.ex_allreduce_epilogue_i64(*ar(0, 0, 1, 8, 8)) == X.EX_ERR_ARG
+    assert L.ex_allreduce_epilogue_i64(*ar(0, 17, 1, 8, 8)) == X.EX_ERR_ARG
     assert L.ex_allreduce_epilogue_i64(*ar(-1, 2, 1, 8, 8)) == X.EX_ERR_ARG
     assert L.ex_allreduce_epilogue_i64(*ar(0, 2, 9, 8, 8)) == X.EX_ERR_DTYPE
     assert L.ex_allreduce_epilogue_i64(*ar(0, 2, 1, 4, 8)) == X.EX_ERR_ARG
     assert L.ex_allreduce_epilogue_i64(*ar(0, 2, 1, 8, 4)) == X.EX_ERR_ARG
     assert L.ex_allreduce_epilogue_i64(*ar(0, 2, 1, 8, 8, M=-1)) == X.EX_ERR_ARG
     assert L.ex_allreduce_epilogue_i64(*ar(0, 2, 1, 8, 8, parts=None)) == X.EX_ERR_ARG
+    assert L.ex_allreduce_epilogue_i64(*ar(0, 2, 1, 8, 8, outs=None)) == X.EX_ERR_ARG
+    assert L.ex_allreduce_epilogue_i64(*ar(0, 2, 1, 9, 9, N=7)) == X.EX_ERR_ALIGN
+    assert L.ex_allreduce_epilogue_i64(*ar(0, 2, 1, 9, 8)) == X.EX_ERR_ALIGN
+    # peer-memory row-maxima exchange + digitize: bad F, dtype, rank / world, rows beyond the exchange slots, NULLs
+    td = lambda F=14, dt=1, rank=0, world=2, rows=4, max_rows=8, xch=p: (p, dt, 64, rows, 64, F, xch, max_rows, p,
+                                                                         rank, world, p, p, 64, p, p, None)
+    assert L.ex_tp_digitize(*td(F=13)) == X.EX_ERR_ARG
+    assert L.ex_tp_digitize(*td(dt=9)) == X.EX_ERR_DTYPE
+    assert L.ex_tp_digitize(*td(rank=2)) == X.EX_ERR_ARG
+    assert L.ex_tp_digitize(*td(world=17)) == X.EX_ERR_ARG
+    assert L.ex_tp_digitize(*td(rows=9)) == X.EX_ERR_ARG
+    assert L.ex_tp_digitize(*td(xch=None)) == X.EX_ERR_ARG
+    assert L.ex_tp_digitize(*td(rows=0)) == X.EX_OK  # empty: every rank skips it alike
     # IPC helpers: NULL arguments are rejected before any driver call
     off = ctypes.c_uint64(0)
     assert L.ex_ipc_get_handle(None, ctypes.create_string_buffer(X.EX_IPC_HANDLE_BYTES), ctypes.byref(off)) == X.EX_ERR_ARG

@@ -133,8 +133,8 @@ def test_config3_k_sharded_on_2_4_8_gpus():
 
 
 def _worker_peer(rank, world, port, root, q):
-    """The fused peer-memory all-reduce + epilogue (PeerEpilogue) against the NCCL path and the 1-GPU result, over
-    enough calls that both partial buffers are reused."""
+    """Row-parallel layers with both exchanges over peer memory (PeerRowParallel) against the NCCL path and the 1-GPU
+    result, over enough calls that every shared buffer is reused, eagerly and replayed from a CUDA graph."""
     import sys
     for p in (root, os.path.join(root, "vllm-exact_b200"), os.path.join(root, "tests", "golden")):
         sys.path.insert(0, p)
@@ -148,7 +148,7 @@ def _worker_peer(rank, world, port, root, q):
     try:
         import recipes as R
         from vllm_exact import kernels as K, parallel as P
-        peer = P.PeerEpilogue(256, 4096)
+        peer = P.PeerRowParallel(256, 4096)
         res = {}
         for it, (M, N, Kd, F, tr) in enumerate([(1, 4096, 4096, 14, True), (16, 4096, 12288, 14, True),
                                                 (64, 1024, 4096, 15, False), (5, 200, 12288, 15, True),
@@ -164,8 +164,8 @@ def _worker_peer(rank, world, port, root, q):
             y_nccl = P.row_parallel_linear(xb[:, a:b], *wd, F, tr)
             y_peer = peer.linear(xb[:, a:b], *wd, F, tr)
             res[it] = (bool(torch.equal(y_peer, ref)), bool(torch.equal(y_nccl, ref)))
-        # CUDA graph: one call captured (NCCL row-max all-reduce included), replayed with new inputs; the epoch lives
-        # on the device, so every replay runs a fresh round of the peer protocol
+        # CUDA graph: one call captured, replayed with new inputs; the epochs live on the device, so every replay runs
+        # a fresh round of both peer protocols
         M, N, Kd = 16, 4096, 12288
         ks = Kd // world
         a, b = rank * ks, (rank + 1) * ks
@@ -211,9 +211,9 @@ def ctypes_code():
     return c.value
 
 
-def test_peer_epilogue_two_or_more_gpus_bitexact():
-    """Row-parallel layers with the fused peer-memory all-reduce + epilogue give the 1-GPU bits (and the NCCL path's)
-    on every rank, for 2 GPUs and, where present, 4 and 8."""
+def test_peer_row_parallel_two_or_more_gpus_bitexact():
+    """Row-parallel layers with both exchanges over peer memory give the 1-GPU bits (and the NCCL path's) on every
+    rank, for 2 GPUs and, where present, 4 and 8."""
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs 2 GPUs")
@@ -238,65 +238,108 @@ def test_peer_epilogue_two_or_more_gpus_bitexact():
             assert all(a and b for a, b in v.values()), (world, r, v)
 
 
-def _one_gpu_peer_args(dev, M, N, world):
+def _one_gpu_peer_args(dev, M, N, world, out_dtype=torch.bfloat16):
     """Device arrays for a single-GPU call of ex_allreduce_epilogue_i64: every 'rank' is this process."""
+    from vllm_exact import _lib
     parts = [torch.randint(-2**40, 2**40, (M, N), dtype=torch.int64, device=dev) for _ in range(world)]
-    flags = torch.zeros(2 * world, dtype=torch.int32, device=dev)
+    outs = [torch.zeros(M, N, dtype=out_dtype, device=dev) for _ in range(world)]
+    flags = torch.zeros(_lib.tp_flag_words(world), dtype=torch.int32, device=dev)
     ctl = torch.zeros(2, dtype=torch.int32, device=dev)
     part_ptrs = torch.tensor([t.data_ptr() for t in parts], dtype=torch.int64, device=dev)
+    out_ptrs = torch.tensor([t.data_ptr() for t in outs], dtype=torch.int64, device=dev)
     flag_ptrs = torch.tensor([flags.data_ptr()] * world, dtype=torch.int64, device=dev)
-    return parts, flags, ctl, part_ptrs, flag_ptrs
+    return parts, outs, flags, ctl, part_ptrs, out_ptrs, flag_ptrs
 
 
-def test_peer_epilogue_one_rank_equals_epilogue():
-    """world = 1: the fused kernel is the plain exact epilogue (bitwise vs ex_epilogue_i64)."""
-    if not torch.cuda.is_available():
-        pytest.skip("needs a GPU")
+def _lib_mod():
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, os.path.join(root, "vllm-exact_b200"))
     from vllm_exact import _lib, kernels as K
+    return _lib, K
+
+
+def test_peer_epilogue_one_rank_equals_epilogue():
+    """world = 1: the reduce-scatter + epilogue + all-gather kernel is the plain exact epilogue (bitwise vs
+    ex_epilogue_i64), over two calls (the device epoch advances, every block passes both flag waits)."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    _lib, K = _lib_mod()
     dev = torch.device("cuda", 0)
     M, N = 33, 1000
-    parts, flags, ctl, part_ptrs, flag_ptrs = _one_gpu_peer_args(dev, M, N, 1)
+    parts, outs, flags, ctl, part_ptrs, out_ptrs, flag_ptrs = _one_gpu_peer_args(dev, M, N, 1)
     sx = torch.randint(10, 20, (M,), dtype=torch.int32, device=dev)
     sw = torch.randint(15, 20, (N,), dtype=torch.int32, device=dev)
-    y = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
-    st = torch.cuda.current_stream().cuda_stream
-    _lib.check("ex_allreduce_epilogue_i64",
-               _lib.lib().ex_allreduce_epilogue_i64(part_ptrs.data_ptr(), N, flag_ptrs.data_ptr(), ctl.data_ptr(),
-                                                    0, 1, sx.data_ptr(), sw.data_ptr(), M, N, y.data_ptr(),
-                                                    _lib.EX_DTYPE_BF16, N, st))
-    ref = torch.empty_like(y)
+    ref = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
     K.exact_epilogue(parts[0], sx, sw, ref)
-    assert torch.equal(y, ref)
-    assert ctypes_code() == 0
-    assert ctl.tolist() == [1, 0] and flags.tolist() == [1, 1]  # epoch advanced on the device, both barriers passed
+    st = torch.cuda.current_stream().cuda_stream
+    for call in (1, 2):
+        y = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=dev)
+        _lib.check("ex_allreduce_epilogue_i64",
+                   _lib.lib().ex_allreduce_epilogue_i64(part_ptrs.data_ptr(), N, out_ptrs.data_ptr(),
+                                                        flag_ptrs.data_ptr(), ctl.data_ptr(), 0, 1, sx.data_ptr(),
+                                                        sw.data_ptr(), M, N, y.data_ptr(), _lib.EX_DTYPE_BF16, N, st))
+        assert torch.equal(y, ref)
+        assert ctypes_code() == 0
+        blocks = min(256, -(-(M * (N // 2)) // 256))
+        f = flags.tolist()
+        assert ctl.tolist() == [call, 0] and f[0] == call  # epoch advanced on the device, ready flag of this call
+        assert f[1:1 + blocks] == [call] * blocks and not any(f[1 + blocks:])  # one done flag per block
 
 
 def test_peer_epilogue_missing_peer_times_out_with_status():
     """Failure detection without a GPU fault: a 'peer' that never signals (a flag nothing sets) makes the bounded
-    waits run out (about 2 s each: the ready wait, then the done wait of the last block); the kernel records
+    waits run out (about 2 s for the first; the others give up once the error is recorded); the kernel records
     EX_DEVERR_WAIT_PEER (6), writes no output and the context stays usable."""
     if not torch.cuda.is_available():
         pytest.skip("needs a GPU")
-    import sys
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    sys.path.insert(0, os.path.join(root, "vllm-exact_b200"))
-    from vllm_exact import _lib
+    _lib, K = _lib_mod()
     dev = torch.device("cuda", 0)
     M, N = 4, 256
-    parts, flags, ctl, part_ptrs, flag_ptrs = _one_gpu_peer_args(dev, M, N, 2)
+    parts, outs, flags, ctl, part_ptrs, out_ptrs, flag_ptrs = _one_gpu_peer_args(dev, M, N, 2, torch.float32)
     sx = torch.full((M,), 12, dtype=torch.int32, device=dev)
     sw = torch.full((N,), 17, dtype=torch.int32, device=dev)
     y = torch.full((M, N), 7.0, dtype=torch.float32, device=dev)
     assert ctypes_code() == 0
     st = torch.cuda.current_stream().cuda_stream
     _lib.check("ex_allreduce_epilogue_i64",
-               _lib.lib().ex_allreduce_epilogue_i64(part_ptrs.data_ptr(), N, flag_ptrs.data_ptr(), ctl.data_ptr(),
-                                                    0, 2, sx.data_ptr(), sw.data_ptr(), M, N, y.data_ptr(),
-                                                    _lib.EX_DTYPE_F32, N, st))
+               _lib.lib().ex_allreduce_epilogue_i64(part_ptrs.data_ptr(), N, out_ptrs.data_ptr(), flag_ptrs.data_ptr(),
+                                                    ctl.data_ptr(), 0, 2, sx.data_ptr(), sw.data_ptr(), M, N,
+                                                    y.data_ptr(), _lib.EX_DTYPE_F32, N, st))
     assert ctypes_code() == 6
     assert bool((y == 7.0).all())  # nothing written
     z = torch.ones(8, device=dev) * 3  # the context still works
     assert float(z.sum()) == 24.0
+
+
+def test_tp_digitize_one_rank_equals_digitize():
+    """world = 1: the row-maxima exchange + digitize kernel gives exactly ex_digitize's digits (F = 14 and 15, bf16 and
+    fp32 rows with an all-zero row and a subnormal-maximum row), over three calls on one set of exchange slots."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a GPU")
+    _lib, K = _lib_mod()
+    dev = torch.device("cuda", 0)
+    max_rows = 64
+    xch = torch.zeros(max_rows, dtype=torch.int64, device=dev)
+    xch_ptrs = torch.tensor([xch.data_ptr()], dtype=torch.int64, device=dev)
+    ctl = torch.zeros(2, dtype=torch.int32, device=dev)
+    st = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator().manual_seed(3)
+    for call, (M, Kd, F, dt) in enumerate([(7, 1000, 14, torch.bfloat16), (64, 1536, 15, torch.float32),
+                                           (3, 4096, 14, torch.bfloat16)], start=1):
+        x = torch.randn(M, Kd, generator=g)
+        x[0] = 0.0
+        if M > 2:
+            x[2] = 0.0
+            x[2, 5] = 1e-40  # subnormal row maximum
+        x = x.to(dt).to(dev)
+        h, l, cs, sh = K._alloc_digits(M, Kd, dev)
+        _lib.check("ex_tp_digitize",
+                   _lib.lib().ex_tp_digitize(x.data_ptr(), K._DT[dt], x.stride(0), M, Kd, F, xch_ptrs.data_ptr(),
+                                             max_rows, ctl.data_ptr(), 0, 1, h.data_ptr(), l.data_ptr(), h.stride(0),
+                                             cs.data_ptr(), sh.data_ptr(), st))
+        ref = K.digitize(x, F)
+        for a, b in zip((h, l, cs, sh), ref):
+            assert torch.equal(a, b), (M, Kd, F, dt)
+        assert ctl.tolist() == [call, 0]
+    assert ctypes_code() == 0

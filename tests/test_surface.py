@@ -10,9 +10,9 @@ import pytest
 ROOT = Path(__file__).resolve().parent.parent
 
 
-def _run(mode, timeout=600):
+def _run(mode, timeout=600, env=None):
     p = subprocess.run([sys.executable, str(ROOT / "tests" / "surface_driver.py"), mode], capture_output=True,
-                       text=True, timeout=timeout, cwd=str(ROOT))
+                       text=True, timeout=timeout, cwd=str(ROOT), env=env)
     lines = [l for l in p.stdout.splitlines() if l.startswith("SURFACE_JSON ")]
     assert p.returncode == 0 and lines, p.stdout[-2000:] + p.stderr[-4000:]
     return json.loads(lines[-1][len("SURFACE_JSON "):])
@@ -31,6 +31,26 @@ def test_enable_returns_reference_kwargs_and_installs_everything():
     assert r["plugin"] == [14, True, True]
     assert "only be called once" in r["second_call"]
     assert r["custom_op"] == "exactmm.linear"
+    assert r["entry_points"] == ["vllm_exact:vllm_plugin"]
+    assert r["plugin_idempotent"] is True
+    assert r["settings_env"] == {"f": 14, "lm_head": True, "attention": True, "max_model_len": 20480,
+                                 "cfg_table": None}
+
+
+def test_general_plugin_applies_settings_in_worker_processes():
+    """vLLM's tensor-parallel workers import vLLM afresh and never run enable(); the package's general-plugin entry
+    point (run by vLLM in every process) applies the settings enable() recorded in the environment."""
+    import os
+    env = dict(os.environ)
+    env["VLLM_EXACT_B200_SETTINGS"] = json.dumps({"f": 15, "lm_head": False, "attention": True,
+                                                  "max_model_len": 4096, "cfg_table": None})
+    env["VLLM_BATCH_INVARIANT"] = "1"
+    r = _run("worker", env=env)
+    assert r["quant_config"] == "vllm_exact.plugin"
+    assert r["fa_forward_file"] == "paged_attn.py"
+    assert r["gdn_invariant"] is True
+    assert r["max_len"] == 4096
+    assert r["plugin"] == [15, False, False, 15]
 
 
 def test_enable_after_vllm_import_is_refused():

@@ -12,6 +12,12 @@ LIB_PATH = Path(os.environ.get("VLLM_EXACT_B200_LIB", Path(__file__).with_name("
 EX_OK, EX_ERR_ARG, EX_ERR_ALIGN, EX_ERR_WORKSPACE, EX_ERR_DTYPE, EX_ERR_UNSUPPORTED, EX_ERR_CUDA, EX_ERR_DEVICE = range(8)
 EX_DTYPE_F32, EX_DTYPE_BF16, EX_DTYPE_F16 = 0, 1, 2
 EX_IPC_HANDLE_BYTES = 64
+EX_TP_MAX_WORLD, EX_TP_MAX_BLOCKS = 16, 256
+
+
+def tp_flag_words(world: int) -> int:
+    """int32 flag words per rank of ex_allreduce_epilogue_i64 (EX_TP_FLAG_WORDS)."""
+    return world + world * EX_TP_MAX_BLOCKS
 EX_ALGO_AUTO, EX_ALGO_SIMT, EX_ALGO_TC_I8 = 0, 1, 2
 EX_LINEAR_STATIC_WEIGHTS = 0x100  # flag OR-ed into algo (vllm_exact_b200.h)
 
@@ -40,8 +46,10 @@ SIGNATURES = {
     "ex_ipc_get_handle": (c_i32, [c_vp, c_vp, ctypes.POINTER(ctypes.c_uint64)]),
     "ex_ipc_open_handle": (c_i32, [c_vp, ctypes.POINTER(c_vp)]),
     "ex_ipc_close_handle": (c_i32, [c_vp]),
-    "ex_allreduce_epilogue_i64": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_i32, c_i32, c_vp, c_vp, c_i64, c_i64, c_vp, c_i32,
-                                          c_i64, c_vp]),
+    "ex_tp_digitize": (c_i32, [c_vp, c_i32, c_i64, c_i64, c_i64, c_i32, c_vp, c_i64, c_vp, c_i32, c_i32, c_vp, c_vp,
+                               c_i64, c_vp, c_vp, c_vp]),
+    "ex_allreduce_epilogue_i64": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_vp, c_i32, c_i32, c_vp, c_vp, c_i64, c_i64, c_vp,
+                                          c_i32, c_i64, c_vp]),
     "ex_paged_decode_workspace_bytes": (c_sz, [c_i32, c_i32, c_i32, c_i32, c_i32]),
     "ex_paged_decode": (c_i32, [c_vp, c_i64, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_i32,
                                 c_i32, c_i32, c_i32, c_i32, c_f32, c_i32, c_i32, c_vp, c_i64, c_i64, c_i32, c_vp, c_sz,

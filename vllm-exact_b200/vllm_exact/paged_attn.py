@@ -110,6 +110,8 @@ def install():
     reference counts those leading decodes on the host (an .item() sync); here the kernel reads query_start_loc and
     finds them itself, so mixed steps are also free of host syncs."""
     from vllm.v1.attention.backends import flash_attn as fa
+    if hasattr(fa.FlashAttentionImpl.forward, "_vllm_exact_b200_orig"):
+        return fa.FlashAttentionImpl.forward._vllm_exact_b200_orig  # already installed (install is idempotent)
     orig = fa.FlashAttentionImpl.forward
     DEC = fa.AttentionType.DECODER
 
@@ -135,6 +137,7 @@ def install():
                          self.scale, out3, nreq, attn_metadata.max_seq_len, query_start_loc=qsl)
         return res
 
+    forward._vllm_exact_b200_orig = orig
     fa.FlashAttentionImpl.forward = forward
     return orig
 

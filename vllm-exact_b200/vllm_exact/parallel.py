@@ -14,9 +14,10 @@ The reference runs on one GPU only (README.md:95). Sharding the exact layer acro
     5. every rank applies the scaling epilogue.
   Steps 1-2 also run once for the weights at load time (the rows of a weight matrix are K-sharded too).
 
-The collectives are torch.distributed calls on the tensor-parallel group (NCCL over NVLink on GPUs). PeerEpilogue
-fuses steps 4 and 5 into one kernel that reads the other ranks' partial totals over NVLink (CUDA IPC mappings) and
-applies the epilogue, without NCCL on the data path. The compute
+The collectives of row_parallel_linear are torch.distributed calls on the tensor-parallel group (NCCL over NVLink on
+GPUs). PeerRowParallel runs the same steps with both exchanges as peer-memory kernels over NVLink (CUDA IPC mappings):
+steps 1-2 in one kernel (row maxima exchanged, slice digitized), steps 4-5 in another (reduce-scatter, epilogue of
+this rank's columns, all-gather of the finished values), without NCCL on the data path. The compute
 steps go through an `ops` object; the product uses the sm_100a library (CudaOps). Tests can pass another `ops` to
 exercise the collective logic on CPU ranks (gloo), the way a fake device layer is used in host tests.
 """
@@ -61,8 +62,9 @@ class CudaOps:
         return K.exact_linear_partial_i64(xd, wd, F, trunc)
 
     @staticmethod
-    def epilogue(tot: torch.Tensor, sx: torch.Tensor, sw: torch.Tensor, dtype) -> torch.Tensor:
-        out = torch.empty(tot.shape, dtype=dtype, device=tot.device)
+    def epilogue(tot: torch.Tensor, sx: torch.Tensor, sw: torch.Tensor, dtype, out=None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty(tot.shape, dtype=dtype, device=tot.device)
         return K.exact_epilogue(tot, sx, sw, out)
 
 
@@ -108,10 +110,10 @@ def digitize_weight_row_sharded(w: torch.Tensor, F: int, group=None, ops=CudaOps
 
 
 def row_parallel_linear(x: torch.Tensor, wh, wl, cw, sw, F: int, trunc: bool, group=None, ops=CudaOps,
-                        out_dtype=None) -> torch.Tensor:
+                        out_dtype=None, out=None) -> torch.Tensor:
     """y = x . w^T for a K-sharded layer: x is this rank's (..., K_local) slice, (wh, wl, cw, sw) its weight digits
     made by digitize_weight_row_sharded. Every rank returns the full (..., N) output, bitwise identical to the 1-GPU
-    exact layer."""
+    exact layer; `out` (M x N, row-major, M = rows of x) receives it when given."""
     g = group if group is not None else _default_group()
     shp = x.shape
     x2 = x.reshape(-1, shp[-1])
@@ -121,42 +123,52 @@ def row_parallel_linear(x: torch.Tensor, wh, wl, cw, sw, F: int, trunc: bool, gr
     xd = ops.digitize_given(x2, F, amax)
     tot = ops.partial(xd, (wh, wl, cw, sw), F, trunc)
     dist.all_reduce(tot, op=dist.ReduceOp.SUM, group=g)
+    if out is not None:
+        return ops.epilogue(tot, xd[3], sw, out.dtype, out=out)
     y = ops.epilogue(tot, xd[3], sw, out_dtype or x.dtype)
     return y.reshape(*shp[:-1], wh.shape[0])
 
 
-class PeerEpilogue:
-    """Fused all-reduce + exact epilogue of K-sharded partial totals over peer memory (ex_allreduce_epilogue_i64), in
-    place of the int64 NCCL all-reduce and the separate epilogue of row_parallel_linear. One object per process group
-    and largest output (max_rows x max_cols): every rank owns one partial buffer, one flag array (2 x world int32) and
-    two control words (the call epoch, kept on the device, so calls can be captured in CUDA graphs); the buffers are
-    shared with the other ranks through CUDA IPC handles exchanged once with all_gather_object (plain peer mappings,
-    no multicast objects). Calls must be issued in the same order on every rank of the group."""
+class PeerRowParallel:
+    """Row-parallel exact layers with both exchange steps over peer memory instead of NCCL: ex_tp_digitize (row
+    maxima of the K slice sent to every rank as (epoch, value) words, whole-row maxima, digits of the slice) and
+    ex_allreduce_epilogue_i64 (reduce-scatter of the int64 partial totals, exact epilogue of this rank's 1/p of the
+    columns, all-gather of the finished values), plain loads and stores over NVLink into buffers shared through CUDA
+    IPC handles exchanged once with all_gather_object (plain peer mappings, no multicast objects). Between the two runs
+    the partial GEMM, written straight into this rank's shared partial buffer.
+
+    One object per process group and largest call (max_rows x max_cols outputs). Same arguments and bitwise the same
+    result as row_parallel_linear. Calls must be issued in the same order on every rank of the group; the epochs live
+    on the device, so calls can be captured in CUDA graphs."""
 
     def __init__(self, max_rows: int, max_cols: int, group=None, device=None):
         g = group if group is not None else _default_group()
         self.group = g
         self.rank, self.world = dist.get_rank(g), dist.get_world_size(g)
+        if self.world > _lib.EX_TP_MAX_WORLD:
+            raise ValueError(f"PeerRowParallel supports up to {_lib.EX_TP_MAX_WORLD} ranks")
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.device = dev
-        self.capacity = max_rows * max_cols
-        self.part = torch.empty(self.capacity, dtype=torch.int64, device=dev)
-        self.flags = torch.zeros(2 * self.world, dtype=torch.int32, device=dev)
-        self.ctl = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.max_rows, self.max_cols = max_rows, max_cols
+        self.xch = torch.zeros(self.world * max_rows, dtype=torch.int64, device=dev)  # (epoch, max) words
+        self.part = torch.zeros(max_rows * max_cols, dtype=torch.int64, device=dev)
+        self.outx = torch.zeros(max_rows * max_cols, dtype=torch.float32, device=dev)  # 4 bytes fit every out dtype
+        self.flags = torch.zeros(_lib.tp_flag_words(self.world), dtype=torch.int32, device=dev)
+        self.ctl = torch.zeros(4, dtype=torch.int32, device=dev)  # [0:2] ex_tp_digitize, [2:4] the all-reduce
         torch.cuda.synchronize(dev)
-        mine = [self._handle(t) for t in (self.part, self.flags)]
+        mine = [self._handle(t) for t in (self.xch, self.part, self.outx, self.flags)]
         every = [None] * self.world
         dist.all_gather_object(every, mine, group=g)
         self._opened = []
         self._bases = {}  # exported allocation handle -> mapped base (tensors may share one allocation)
-        ptrs = []  # ptrs[p] = (partial, flags) device addresses of rank p, as seen from this GPU
+        ptrs = []  # ptrs[p] = device addresses of rank p's buffers, as seen from this GPU
         for p, hs in enumerate(every):
             if p == self.rank:
-                ptrs.append([self.part.data_ptr(), self.flags.data_ptr()])
+                ptrs.append([t.data_ptr() for t in (self.xch, self.part, self.outx, self.flags)])
             else:
                 ptrs.append([self._open(h) + off for h, off in hs])
-        self.part_ptrs = torch.tensor([ptrs[p][0] for p in range(self.world)], dtype=torch.int64, device=dev)
-        self.flag_ptrs = torch.tensor([ptrs[p][1] for p in range(self.world)], dtype=torch.int64, device=dev)
+        self.xch_ptrs, self.part_ptrs, self.outx_ptrs, self.flag_ptrs = (
+            torch.tensor([ptrs[p][k] for p in range(self.world)], dtype=torch.int64, device=dev) for k in range(4))
         torch.cuda.synchronize(dev)
         dist.barrier(group=g)  # every rank has mapped every buffer before the first call
 
@@ -187,25 +199,34 @@ class PeerEpilogue:
         self._opened = []
         self._bases = {}
 
-    def linear(self, x: torch.Tensor, wh, wl, cw, sw, F: int, trunc: bool, out_dtype=None) -> torch.Tensor:
-        """row_parallel_linear with the partial total written into this rank's shared buffer and the all-reduce and
-        epilogue fused over peer memory. Same arguments and bitwise the same result."""
+    def linear(self, x: torch.Tensor, wh, wl, cw, sw, F: int, trunc: bool, out_dtype=None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+        """row_parallel_linear with both exchanges over peer memory: same arguments and bitwise the same result."""
         shp = x.shape
         x2 = x.reshape(-1, shp[-1])
         if x2.stride(-1) != 1:
             x2 = x2.contiguous()
-        M, N = x2.shape[0], wh.shape[0]
-        if M * N > self.capacity:
-            raise ValueError(f"PeerEpilogue holds {self.capacity} outputs, the call needs {M * N}")
-        amax = global_row_absmax(x2, self.group, CudaOps)
-        xd = CudaOps.digitize_given(x2, F, amax)
+        M, Kd = x2.shape
+        N = wh.shape[0]
+        if M > self.max_rows or N > self.max_cols:
+            raise ValueError(f"PeerRowParallel holds {self.max_rows} x {self.max_cols} outputs, the call needs "
+                             f"{M} x {N}")
+        dev = x2.device
+        st = K._stream(dev)
+        h, l, cs, sh = K._alloc_digits(M, Kd, dev)
+        ctl = self.ctl.data_ptr()
+        with torch.cuda.device(dev):
+            check("ex_tp_digitize",
+                  lib().ex_tp_digitize(x2.data_ptr(), K._DT[x2.dtype], x2.stride(0), M, Kd, F,
+                                       self.xch_ptrs.data_ptr(), self.max_rows, ctl, self.rank, self.world,
+                                       h.data_ptr(), l.data_ptr(), h.stride(0), cs.data_ptr(), sh.data_ptr(), st))
         part = self.part[: M * N].view(M, N)
-        K.exact_linear_partial_i64(xd, (wh, wl, cw, sw), F, trunc, out=part)
-        y = torch.empty(M, N, dtype=out_dtype or x.dtype, device=x2.device)
-        with torch.cuda.device(x2.device):
+        K.exact_linear_partial_i64((h, l, cs, sh), (wh, wl, cw, sw), F, trunc, out=part)
+        y = out if out is not None else torch.empty(M, N, dtype=out_dtype or x.dtype, device=dev)
+        with torch.cuda.device(dev):
             check("ex_allreduce_epilogue_i64",
-                  lib().ex_allreduce_epilogue_i64(self.part_ptrs.data_ptr(), N, self.flag_ptrs.data_ptr(),
-                                                  self.ctl.data_ptr(), self.rank, self.world, xd[3].data_ptr(),
-                                                  sw.data_ptr(), M, N, y.data_ptr(), K._DT[y.dtype], y.stride(0),
-                                                  K._stream(x2.device)))
-        return y.reshape(*shp[:-1], N)
+                  lib().ex_allreduce_epilogue_i64(self.part_ptrs.data_ptr(), N, self.outx_ptrs.data_ptr(),
+                                                  self.flag_ptrs.data_ptr(), ctl + 8, self.rank, self.world,
+                                                  sh.data_ptr(), sw.data_ptr(), M, N, y.data_ptr(), K._DT[y.dtype],
+                                                  y.stride(0), st))
+        return y if out is not None else y.reshape(*shp[:-1], N)
