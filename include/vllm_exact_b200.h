@@ -185,19 +185,21 @@ int ex_ipc_close_handle(void* base);
  * ex_epilogue_i64). Every rank of the group makes the same calls in the same order; ranks run on different GPUs (the
  * kernels wait for one another). Buffers named "of every rank" are device arrays of `world` pointers, index p = rank
  * p's buffer as mapped on this GPU (e.g. with ex_ipc_open_handle), this rank's at index `rank`; all of them are
- * zero-filled once before the first call. Epochs live in the ctl words on the device, so calls can be captured in a
- * CUDA graph. A wait that runs out (EX_WAIT_TIMEOUT, about 2 s) records a device error (ex_device_error) and the call
- * finishes with wrong outputs. Neither kernel depends on all of its own blocks being resident at once.
+ * zero-filled once before the first call. Values cross GPUs as 64-bit words (call epoch << 32 | payload) that the
+ * reader polls, so no fence is needed. Epochs live in the ctl words on the device, so calls can be captured in a CUDA
+ * graph. Both kernels are launched with programmatic dependent launch. A wait that runs out (about 2 s) records a
+ * device error (ex_device_error) and the call finishes with wrong outputs. Neither kernel depends on all of its own
+ * blocks being resident at once.
  */
 #define EX_TP_MAX_WORLD 16
 #define EX_TP_MAX_BLOCKS 256
 /* int32 flag words per rank of ex_allreduce_epilogue_i64 */
-#define EX_TP_FLAG_WORDS(world) ((world) + (world) * EX_TP_MAX_BLOCKS)
+#define EX_TP_FLAG_WORDS(world) (world)
 
 /* ex_tp_digitize: row maxima of this rank's K slice x (rows x K) sent to every rank, whole-row maxima taken, and the
  * slice digitized with them: bitwise the K slice of the digits of the whole rows (semantics of digitize_torch,
  * src/vllm_exact/kernels.py:22-39; for F = 15, cs is the slice's row sum).
- *   xch   of every rank: uint64 exchange slots [world][max_rows] (call epoch << 32 | float bits of a maximum)
+ *   xch   of every rank: 64-bit exchange words [world][max_rows]
  *   ctl   this rank's two int32 words for this kernel (epoch, block counter) */
 int ex_tp_digitize(const void* x, int x_dtype, int64_t ldx, int64_t rows, int64_t K, int F, const void* xch,
                    int64_t max_rows, int32_t* ctl, int rank, int world, int8_t* h, int8_t* l, int64_t ldd, int32_t* cs,
@@ -207,12 +209,13 @@ int ex_tp_digitize(const void* x, int x_dtype, int64_t ldx, int64_t rows, int64_
  * ex_epilogue_i64) and written to this rank's `out`, as a reduce-scatter (rank r sums and finishes columns
  * [r N / world, (r + 1) N / world), rounded down to even) followed by an all-gather of the finished values.
  *   parts  of every rank: (M, N) int64 partial, leading dimension ldt
- *   outs   of every rank: (M, N) output exchange buffer of out_dtype elements, leading dimension N
+ *   xch    of every rank: output exchange buffer of 64-bit words, M * N / 2 of them for bf16/fp16 outputs, M * N for
+ *          fp32 outputs
  *   flags  of every rank: EX_TP_FLAG_WORDS(world) int32 words
  *   ctl    this rank's two int32 words for this kernel
- * N, ldt and ldo must be even (EX_ERR_ALIGN otherwise). When the call completes, every rank has finished reading this
- * rank's partial and writing into its exchange buffer, so both may be reused by the next work on the stream. */
-int ex_allreduce_epilogue_i64(const void* parts, int64_t ldt, const void* outs, const void* flags, int32_t* ctl,
+ * N, ldt and ldo must be even (EX_ERR_ALIGN otherwise). When the call completes on every rank, every rank has
+ * finished reading this rank's partial, so it may be rewritten by the next work on the stream. */
+int ex_allreduce_epilogue_i64(const void* parts, int64_t ldt, const void* xch, const void* flags, int32_t* ctl,
                               int rank, int world, const int32_t* sx, const int32_t* sw, int64_t M, int64_t N,
                               void* out, int out_dtype, int64_t ldo, void* stream);
 

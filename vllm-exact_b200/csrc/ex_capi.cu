@@ -452,10 +452,11 @@ int ex_tp_digitize(const void* x, int x_dtype, int64_t ldx, int64_t rows, int64_
   const int blocks = (int)std::min<int64_t>(rows, 4 * (int64_t)num_sms());
   cudaStream_t st = (cudaStream_t)stream;
   unsigned long long* const* xp = reinterpret_cast<unsigned long long* const*>(xch);
-#define EX_TPD(T, FF)                                                                                          \
-  ex::k_tp_digitize<T, FF><<<blocks, ex::DIG_THREADS, 0, st>>>(reinterpret_cast<const T*>(x), ldx, (int)rows, \
-                                                                 (int)K, xp, ctl, rank, world, (int)max_rows, h, l, \
-                                                                 ldd, cs, sh)
+  cudaError_t e = cudaSuccess;
+#define EX_TPD(T, FF)                                                                                              \
+  e = ex_launch_pdl(ex::k_tp_digitize<T, FF>, dim3(blocks), dim3(ex::DIG_THREADS), 0, st,                          \
+                    reinterpret_cast<const T*>(x), ldx, (int)rows, (int)K, xp, ctl, rank, world, (int)max_rows, h, l, \
+                    ldd, cs, sh)
   if (x_dtype == EX_DTYPE_F32) {
     if (F == 15) EX_TPD(float, 15); else EX_TPD(float, 14);
   } else if (x_dtype == EX_DTYPE_BF16) {
@@ -464,28 +465,30 @@ int ex_tp_digitize(const void* x, int x_dtype, int64_t ldx, int64_t rows, int64_
     if (F == 15) EX_TPD(__half, 15); else EX_TPD(__half, 14);
   }
 #undef EX_TPD
-  return cuda_status(cudaGetLastError());
+  return cuda_status(e);
 }
 
-int ex_allreduce_epilogue_i64(const void* parts, int64_t ldt, const void* outs, const void* flags, int32_t* ctl,
+int ex_allreduce_epilogue_i64(const void* parts, int64_t ldt, const void* xch, const void* flags, int32_t* ctl,
                               int rank, int world, const int32_t* sx, const int32_t* sw, int64_t M, int64_t N,
                               void* out, int out_dtype, int64_t ldo, void* stream) {
   if (M < 0 || N < 0 || M > INT32_MAX || N > INT32_MAX) return EX_ERR_ARG;
   if (world < 1 || world > ex::TPF_MAX_WORLD || rank < 0 || rank >= world) return EX_ERR_ARG;
   if (!dtype_ok(out_dtype)) return EX_ERR_DTYPE;
-  if (!parts || !outs || !flags || !ctl || !sx || !sw || !out || ldt < N || ldo < N) return EX_ERR_ARG;
+  if (!parts || !xch || !flags || !ctl || !sx || !sw || !out || ldt < N || ldo < N) return EX_ERR_ARG;
   if (N % 2 != 0 || ldt % 2 != 0 || ldo % 2 != 0) return EX_ERR_ALIGN;  // column pairs: 16-byte partial loads
-  // every rank takes part in every call, also for an empty output (one block then only runs the barriers). The block
-  // count depends on (M, N, world) only, so it is the same on every rank: block b pairs with block b of the others.
+  // every rank takes part in every call, also for an empty output (one block then only exchanges the flags). The
+  // block count depends on (M, N, world) only, so it is the same on every rank: block b pairs with block b of the
+  // others; at most TPF_MAX_BLOCKS small blocks, all resident together.
   const int64_t pairs = M * cdiv(N, 2 * (int64_t)world);
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(pairs, ex::TPF_THREADS), ex::TPF_MAX_BLOCKS));
   cudaStream_t st = (cudaStream_t)stream;
   const long long* const* pp = reinterpret_cast<const long long* const*>(parts);
-  void* const* op = reinterpret_cast<void* const*>(outs);
+  unsigned long long* const* xp = reinterpret_cast<unsigned long long* const*>(xch);
   int* const* fp = reinterpret_cast<int* const*>(flags);
-#define EX_TPF_LAUNCH(OD)                                                                                          \
-  ex::k_tp_allreduce_epilogue<OD><<<blocks, ex::TPF_THREADS, 0, st>>>(pp, ldt, op, fp, ctl, rank, world, sx, sw,   \
-                                                                       (int)M, (int)N, out, ldo)
+  cudaError_t e;
+#define EX_TPF_LAUNCH(OD)                                                                                        \
+  e = ex_launch_pdl(ex::k_tp_allreduce_epilogue<OD>, dim3(blocks), dim3(ex::TPF_THREADS), 0, st, pp, ldt, xp, fp, \
+                    ctl, rank, world, sx, sw, (int)M, (int)N, out, ldo)
   if (out_dtype == EX_DTYPE_F32)
     EX_TPF_LAUNCH(EX_DTYPE_F32);
   else if (out_dtype == EX_DTYPE_BF16)
@@ -493,7 +496,7 @@ int ex_allreduce_epilogue_i64(const void* parts, int64_t ldt, const void* outs, 
   else
     EX_TPF_LAUNCH(EX_DTYPE_F16);
 #undef EX_TPF_LAUNCH
-  return cuda_status(cudaGetLastError());
+  return cuda_status(e);
 }
 
 size_t ex_paged_decode_workspace_bytes(int n, int H, int D, int max_len, int split) {

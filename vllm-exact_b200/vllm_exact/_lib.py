@@ -17,7 +17,7 @@ EX_TP_MAX_WORLD, EX_TP_MAX_BLOCKS = 16, 256
 
 def tp_flag_words(world: int) -> int:
     """int32 flag words per rank of ex_allreduce_epilogue_i64 (EX_TP_FLAG_WORDS)."""
-    return world + world * EX_TP_MAX_BLOCKS
+    return world
 EX_ALGO_AUTO, EX_ALGO_SIMT, EX_ALGO_TC_I8 = 0, 1, 2
 EX_LINEAR_STATIC_WEIGHTS = 0x100  # flag OR-ed into algo (vllm_exact_b200.h)
 

@@ -1,8 +1,14 @@
-"""The torch custom op ``exactmm::linear`` (reference src/vllm_exact/plugin.py:51-69), without any vLLM import.
+"""The torch custom ops of the exact linear layer, without any vLLM import.
 
-Same name, signature and semantics as the reference: x (*, K) bf16/fp16 activations and the digitized weight buffers
-(wh, wl, cw, sw) -> (*, N) in x's dtype. Rows are processed in blocks of RB (rows are independent, so the block size
-never changes results). The body calls the sm_100a library: digitize, then the exact GEMM with fused epilogue.
+``exactmm::linear`` (reference src/vllm_exact/plugin.py:51-69): same name, signature and semantics as the reference:
+x (*, K) bf16/fp16 activations and the digitized weight buffers (wh, wl, cw, sw) -> (*, N) in x's dtype. Rows are
+processed in blocks of RB (rows are independent, so the block size never changes results). The body calls the sm_100a
+library: digitize, then the exact GEMM with fused epilogue.
+
+``exactmm::linear_row_parallel`` (no reference counterpart: the reference runs on one GPU): the same for a K-sharded
+(row-parallel) layer of a tensor-parallel group, x being this rank's K slice; the exchange steps of
+parallel.row_parallel_linear run inside the op, so torch.compile sees one opaque call, as for the 1-GPU op.
+
 F and TRUNC are set by vllm_exact.enable().
 """
 import torch
@@ -32,5 +38,24 @@ def exact_linear_op(x: torch.Tensor, wh: torch.Tensor, wl: torch.Tensor, cw: tor
 
 
 @exact_linear_op.register_fake
+def _(x, wh, wl, cw, sw):
+    return x.new_empty(*x.shape[:-1], wh.shape[0])
+
+
+@torch.library.custom_op("exactmm::linear_row_parallel", mutates_args=())
+def exact_linear_row_parallel_op(x: torch.Tensor, wh: torch.Tensor, wl: torch.Tensor, cw: torch.Tensor,
+                                 sw: torch.Tensor) -> torch.Tensor:
+    from . import parallel
+    shp = x.shape
+    N = wh.shape[0]
+    x2 = x.reshape(-1, shp[-1])
+    M = x2.shape[0]
+    out = x.new_empty(M, N)
+    for i in range(0, M, RB):  # every rank holds the same rows, so every rank makes the same collective calls
+        parallel.row_parallel_linear(x2[i:i + RB], wh, wl, cw, sw, F, TRUNC, out=out[i:i + RB])
+    return out.reshape(*shp[:-1], N)
+
+
+@exact_linear_row_parallel_op.register_fake
 def _(x, wh, wl, cw, sw):
     return x.new_empty(*x.shape[:-1], wh.shape[0])

@@ -133,9 +133,9 @@ class PeerRowParallel:
     """Row-parallel exact layers with both exchange steps over peer memory instead of NCCL: ex_tp_digitize (row
     maxima of the K slice sent to every rank as (epoch, value) words, whole-row maxima, digits of the slice) and
     ex_allreduce_epilogue_i64 (reduce-scatter of the int64 partial totals, exact epilogue of this rank's 1/p of the
-    columns, all-gather of the finished values), plain loads and stores over NVLink into buffers shared through CUDA
-    IPC handles exchanged once with all_gather_object (plain peer mappings, no multicast objects). Between the two runs
-    the partial GEMM, written straight into this rank's shared partial buffer.
+    columns, all-gather of the finished values as (epoch, value) words), plain loads and stores over NVLink into
+    buffers shared through CUDA IPC handles exchanged once with all_gather_object (plain peer mappings, no multicast
+    objects). Between the two runs the partial GEMM, written straight into this rank's shared partial buffer.
 
     One object per process group and largest call (max_rows x max_cols outputs). Same arguments and bitwise the same
     result as row_parallel_linear. Calls must be issued in the same order on every rank of the group; the epochs live
@@ -152,7 +152,7 @@ class PeerRowParallel:
         self.max_rows, self.max_cols = max_rows, max_cols
         self.xch = torch.zeros(self.world * max_rows, dtype=torch.int64, device=dev)  # (epoch, max) words
         self.part = torch.zeros(max_rows * max_cols, dtype=torch.int64, device=dev)
-        self.outx = torch.zeros(max_rows * max_cols, dtype=torch.float32, device=dev)  # 4 bytes fit every out dtype
+        self.outx = torch.zeros(max_rows * max_cols, dtype=torch.int64, device=dev)  # epoch words (fp32: one each)
         self.flags = torch.zeros(_lib.tp_flag_words(self.world), dtype=torch.int32, device=dev)
         self.ctl = torch.zeros(4, dtype=torch.int32, device=dev)  # [0:2] ex_tp_digitize, [2:4] the all-reduce
         torch.cuda.synchronize(dev)

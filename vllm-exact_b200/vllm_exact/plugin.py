@@ -78,11 +78,9 @@ def drop_bf16_weight(layer):
 
 
 def _apply(layer, x, bias):
-    if _is_row_sharded(layer):
-        from . import parallel
-        y = parallel.row_parallel_linear(x, layer.ex_wh, layer.ex_wl, layer.ex_cw, layer.ex_sw, F, TRUNC)
-    else:
-        y = torch.ops.exactmm.linear(x, layer.ex_wh, layer.ex_wl, layer.ex_cw, layer.ex_sw)
+    # one opaque custom op per call in both cases, so torch.compile never traces into the library's ctypes calls
+    op = torch.ops.exactmm.linear_row_parallel if _is_row_sharded(layer) else torch.ops.exactmm.linear
+    y = op(x, layer.ex_wh, layer.ex_wl, layer.ex_cw, layer.ex_sw)
     return y if bias is None else y + bias
 
 
