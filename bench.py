@@ -48,8 +48,8 @@ METRIC = "exact-GEMM TB/s (exact_int8 linear, decode shapes M<=64 of the configs
 WORKLOAD = ("configs[1] decode sweep: M in {1,16,64} x (K,N) in {(4096,6144),(4096,4096),(4096,24576),"
             "(12288,4096),(4096,151936)}, F=14 truncated, bf16 out")
 # DRAM bytes (read + write) per k_exact_tc_i8 launch, averaged over the 15 launches of one decode step, from the ncu
-# capture summarised in profiles/k_exact_tc_i8__decode_sweep.md (1.009 x the algorithmic bytes).
-GEMM_TRAFFIC_PER_LAUNCH = 331_717_905
+# capture summarised in profiles/k_exact_tc_i8__decode_sweep.md (1.007 x the algorithmic bytes).
+GEMM_TRAFFIC_PER_LAUNCH = 331_005_542
 
 
 def peaks():
@@ -337,6 +337,8 @@ def run_ours(args):
             torch.cuda.empty_cache()
             result["decode_step"] = decode_step_bench(dev)
             result["cpu_baseline"] = cpu_baseline()
+            torch.cuda.empty_cache()
+            result["engine"] = engine_both_arms()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -1097,6 +1099,32 @@ def _register_engine_model():
         get_mamba_state_copy_func = classmethod(VL.get_mamba_state_copy_func.__func__)
 
     ModelRegistry.register_model("HybridQwen35ForCausalLM", HybridQwen35ForCausalLM)
+
+
+def engine_both_arms(timeout_s=1200):
+    """BASELINE configs[4] through the real vLLM engine, both arms (exact_int8 with the attention patch, and plain
+    non-invariant bf16 vLLM), each in a subprocess running `bench.py --case engine:<arm>` (enable() must run before
+    vLLM is imported, so one arm per process). Returns the step times, their ratio and the exact arm's invariance
+    counts; an arm that fails or runs out of time is reported as such instead of its numbers."""
+    out = {"method": "reference scripts/check_invariance.py: step = (t(321 new tokens) - t(65)) / 256, min of two "
+                     "runs each; invariance = 16 targets with 1,024-token prompts alone vs interleaved in a batch of "
+                     "64 vs alone again, 256 tokens, greedy and T = 1.0; vLLM 0.22, dummy weights, 32 layers"}
+    for arm in ("exact", "plain"):
+        t0 = time.time()
+        try:
+            p = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--case", f"engine:{arm}"],
+                               capture_output=True, text=True, timeout=timeout_s, cwd=str(ROOT))
+            lines = [l for l in p.stdout.splitlines() if l.startswith("ENGINE_JSON ")]
+            if p.returncode != 0 or not lines:
+                out[arm] = {"error": f"exit {p.returncode}: " + (p.stderr.strip().splitlines() or ["?"])[-1][-300:]}
+            else:
+                out[arm] = json.loads(lines[-1][len("ENGINE_JSON "):])
+        except subprocess.TimeoutExpired:
+            out[arm] = {"error": f"timed out after {timeout_s} s"}
+        out[arm]["wall_s"] = round(time.time() - t0, 1)
+    ex, pl = out["exact"].get("speed", {}), out["plain"].get("speed", {})
+    out["overhead"] = {k: round(ex[k]["step_ms"] / pl[k]["step_ms"] - 1, 3) for k in ex if k in pl}
+    return out
 
 
 def engine_case(args):
