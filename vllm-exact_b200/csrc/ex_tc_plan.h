@@ -173,6 +173,17 @@ inline TcPlan tc_plan_bt(int64_t M, int64_t N, int64_t K, int split_k, int sms, 
     // qkv M=256 34.6 -> 26.6 us) and is not taken for wide ones (gate_up, lm_head), where it would not apply.
     const int64_t s = fit / p.n_tiles;
     if (s >= 1 && (int64_t)p.n_tiles * s * 10 >= fit * 6) groups = (int64_t)p.n_tiles * s;
+    // More n-tiles than resident groups, with sibling m-tiles (tensor-bound sizes): whole tiles per group when a
+    // divisor of n_tiles keeps >= 60 % of the groups busy with at most 3 tiles each, since the balanced partition
+    // would split nearly every tile. Measured on B200: gate_up M = 256 78.1 -> 67.7 us, in_proj_qkvz (N = 12288)
+    // M = 256 51.5 -> 47.8 us, o_proj M = 1024 59.5 -> 46.9 us, M = 4096 189 -> 164 us; with 6-12 tiles per group
+    // (gate_up, in_proj_qkvz at M >= 1024) it was 2-10 % slower, so those keep the balanced partition.
+    if (s == 0 && p.gs >= 2)
+      for (int64_t g = fit; g * 10 >= fit * 6; --g)
+        if (p.n_tiles % g == 0 && p.n_tiles / g <= 3) {
+          groups = g;
+          break;
+        }
   }
   groups = std::max<int64_t>(1, std::min<int64_t>(groups, p.T));
   groups = std::min<int64_t>(groups, 2147483647 / p.gs);
