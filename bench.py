@@ -505,6 +505,20 @@ def run_tp(args, dev, rank, world, local):
             gl = graph_of(lambda: [layer(M, name, path) for _ in range(10)])
             row[path] = round(timed(gl, 5) * 100, 2)
             del gl
+        if name in ROW_PARALLEL:
+            # the peer path's three launches, each timed alone (10 back to back per graph): maxima exchange +
+            # digitize, partial GEMM into the shared buffer, reduce-scatter + epilogue + all-gather
+            xd = peer.digitize(XS[(M, name)], 14)
+            part = peer.partial(M, N)
+            parts = {}
+            for step_name, fn in (("exchange_digitize", lambda: peer.digitize(XS[(M, name)], 14, out=xd)),
+                                  ("partial_gemm", lambda: KK.exact_linear_partial_i64(xd, W[name], 14, True,
+                                                                                       out=part)),
+                                  ("reduce_epilogue", lambda: peer.reduce(M, N, xd[3], W[name][3], Y[(M, name)]))):
+                gl = graph_of(lambda: [fn() for _ in range(10)])
+                parts[step_name] = round(timed(gl, 5) * 100, 2)
+                del gl
+            row["peer_launches"] = parts
         per_layer[f"{name}/M{M}"] = row if name in ROW_PARALLEL else row["peer"]
     for M in DECODE_M:
         amax = torch.ones(M, device=dev)

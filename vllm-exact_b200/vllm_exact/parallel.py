@@ -199,6 +199,41 @@ class PeerRowParallel:
         self._opened = []
         self._bases = {}
 
+    def digitize(self, x2: torch.Tensor, F: int, out=None):
+        """Step 1 (ex_tp_digitize): this rank's K slice x2 (M x K_local, row-major) digitized with the whole-row
+        maxima of all ranks. Every rank must call it with the same M."""
+        M, Kd = x2.shape
+        if M > self.max_rows:
+            raise ValueError(f"PeerRowParallel holds {self.max_rows} rows, the call has {M}")
+        dev = x2.device
+        h, l, cs, sh = out if out is not None else K._alloc_digits(M, Kd, dev)
+        with torch.cuda.device(dev):
+            check("ex_tp_digitize",
+                  lib().ex_tp_digitize(x2.data_ptr(), K._DT[x2.dtype], x2.stride(0), M, Kd, F,
+                                       self.xch_ptrs.data_ptr(), self.max_rows, self.ctl.data_ptr(), self.rank,
+                                       self.world, h.data_ptr(), l.data_ptr(), h.stride(0), cs.data_ptr(),
+                                       sh.data_ptr(), K._stream(dev)))
+        return h, l, cs, sh
+
+    def partial(self, M: int, N: int) -> torch.Tensor:
+        """This rank's shared int64 partial buffer, as an (M, N) view: the partial GEMM writes here."""
+        if M > self.max_rows or N > self.max_cols:
+            raise ValueError(f"PeerRowParallel holds {self.max_rows} x {self.max_cols} outputs, the call needs "
+                             f"{M} x {N}")
+        return self.part[: M * N].view(M, N)
+
+    def reduce(self, M: int, N: int, sx: torch.Tensor, sw: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Step 3 (ex_allreduce_epilogue_i64): the partials every rank wrote into its partial(M, N) summed, scaled
+        and written to `out` (M x N, row-major, bf16/fp16/fp32)."""
+        dev = out.device
+        with torch.cuda.device(dev):
+            check("ex_allreduce_epilogue_i64",
+                  lib().ex_allreduce_epilogue_i64(self.part_ptrs.data_ptr(), N, self.outx_ptrs.data_ptr(),
+                                                  self.flag_ptrs.data_ptr(), self.ctl.data_ptr() + 8, self.rank,
+                                                  self.world, sx.data_ptr(), sw.data_ptr(), M, N, out.data_ptr(),
+                                                  K._DT[out.dtype], out.stride(0), K._stream(dev)))
+        return out
+
     def linear(self, x: torch.Tensor, wh, wl, cw, sw, F: int, trunc: bool, out_dtype=None,
                out: torch.Tensor | None = None) -> torch.Tensor:
         """row_parallel_linear with both exchanges over peer memory: same arguments and bitwise the same result."""
@@ -206,27 +241,11 @@ class PeerRowParallel:
         x2 = x.reshape(-1, shp[-1])
         if x2.stride(-1) != 1:
             x2 = x2.contiguous()
-        M, Kd = x2.shape
+        M = x2.shape[0]
         N = wh.shape[0]
-        if M > self.max_rows or N > self.max_cols:
-            raise ValueError(f"PeerRowParallel holds {self.max_rows} x {self.max_cols} outputs, the call needs "
-                             f"{M} x {N}")
-        dev = x2.device
-        st = K._stream(dev)
-        h, l, cs, sh = K._alloc_digits(M, Kd, dev)
-        ctl = self.ctl.data_ptr()
-        with torch.cuda.device(dev):
-            check("ex_tp_digitize",
-                  lib().ex_tp_digitize(x2.data_ptr(), K._DT[x2.dtype], x2.stride(0), M, Kd, F,
-                                       self.xch_ptrs.data_ptr(), self.max_rows, ctl, self.rank, self.world,
-                                       h.data_ptr(), l.data_ptr(), h.stride(0), cs.data_ptr(), sh.data_ptr(), st))
-        part = self.part[: M * N].view(M, N)
-        K.exact_linear_partial_i64((h, l, cs, sh), (wh, wl, cw, sw), F, trunc, out=part)
-        y = out if out is not None else torch.empty(M, N, dtype=out_dtype or x.dtype, device=dev)
-        with torch.cuda.device(dev):
-            check("ex_allreduce_epilogue_i64",
-                  lib().ex_allreduce_epilogue_i64(self.part_ptrs.data_ptr(), N, self.outx_ptrs.data_ptr(),
-                                                  self.flag_ptrs.data_ptr(), ctl + 8, self.rank, self.world,
-                                                  sh.data_ptr(), sw.data_ptr(), M, N, y.data_ptr(), K._DT[y.dtype],
-                                                  y.stride(0), st))
+        part = self.partial(M, N)
+        xd = self.digitize(x2, F)
+        K.exact_linear_partial_i64(xd, (wh, wl, cw, sw), F, trunc, out=part)
+        y = out if out is not None else torch.empty(M, N, dtype=out_dtype or x.dtype, device=x2.device)
+        self.reduce(M, N, xd[3], sw, y)
         return y if out is not None else y.reshape(*shp[:-1], N)
