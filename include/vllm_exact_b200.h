@@ -199,7 +199,8 @@ int ex_ipc_close_handle(void* base);
 /* ex_tp_digitize: row maxima of this rank's K slice x (rows x K) sent to every rank, whole-row maxima taken, and the
  * slice digitized with them: bitwise the K slice of the digits of the whole rows (semantics of digitize_torch,
  * src/vllm_exact/kernels.py:22-39; for F = 15, cs is the slice's row sum).
- *   xch   of every rank: 64-bit exchange words [world][max_rows]
+ *   xch   of every rank: 64-bit exchange words [2][world][max_rows] (two halves by call parity, so back-to-back calls
+ *         of this kernel alone are safe)
  *   ctl   this rank's two int32 words for this kernel (epoch, block counter) */
 int ex_tp_digitize(const void* x, int x_dtype, int64_t ldx, int64_t rows, int64_t K, int F, const void* xch,
                    int64_t max_rows, int32_t* ctl, int rank, int world, int8_t* h, int8_t* l, int64_t ldd, int32_t* cs,

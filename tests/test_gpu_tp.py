@@ -192,6 +192,18 @@ def _worker_peer(rank, world, port, root, q):
             torch.cuda.synchronize(dev)
             res[f"graph{t}"] = (bool(torch.equal(yg, ref)), True)
         del g
+        # the maxima exchange alone, many calls back to back without a synchronization (ranks drift apart): every
+        # call's digits equal the slice of the whole rows' digits
+        M, Kd = 48, 8192
+        ks = Kd // world
+        a, b = rank * ks, (rank + 1) * ks
+        x = torch.randn(M, Kd, generator=torch.Generator().manual_seed(11)).bfloat16().to(dev)
+        ref = [t[:, a:b] if t.dim() == 2 else t for t in K.digitize(x, 14)]
+        xs = x[:, a:b].contiguous()
+        outs = [peer.digitize(xs, 14) for _ in range(20)]
+        torch.cuda.synchronize()
+        res["digitize_back_to_back"] = (all(torch.equal(o[0], ref[0]) and torch.equal(o[1], ref[1]) and
+                                            torch.equal(o[3], ref[3]) for o in outs), True)
         torch.cuda.synchronize()
         code = ctypes_code()
         q.put((rank, res, code))
@@ -319,7 +331,7 @@ def test_tp_digitize_one_rank_equals_digitize():
     _lib, K = _lib_mod()
     dev = torch.device("cuda", 0)
     max_rows = 64
-    xch = torch.zeros(max_rows, dtype=torch.int64, device=dev)
+    xch = torch.zeros(2 * max_rows, dtype=torch.int64, device=dev)
     xch_ptrs = torch.tensor([xch.data_ptr()], dtype=torch.int64, device=dev)
     ctl = torch.zeros(2, dtype=torch.int32, device=dev)
     st = torch.cuda.current_stream().cuda_stream

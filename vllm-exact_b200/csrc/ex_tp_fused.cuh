@@ -10,8 +10,8 @@
 // writer's outstanding memory traffic; an earlier design with a release store per value and a system fence per block
 // was slower than NCCL).
 //
-// k_tp_digitize: row maxima of this rank's K slice -> slot [rank][row] of every rank's exchange buffer -> whole-row
-//   maxima -> digits of the slice.
+// k_tp_digitize: row maxima of this rank's K slice -> slot [epoch parity][rank][row] of every rank's exchange buffer
+//   -> whole-row maxima -> digits of the slice. Safe for back-to-back calls on its own (two halves by epoch parity).
 // k_tp_allreduce_epilogue: reduce-scatter + exact epilogue + all-gather of the int64 partial totals. Rank r owns the
 //   output columns [r N / p, (r + 1) N / p) (rounded down to even): after one flag exchange saying every rank's
 //   partial is complete, it sums the p partials of its columns (peer loads; integer addition is exact in any order),
@@ -124,6 +124,10 @@ __global__ void __launch_bounds__(DIG_THREADS) k_tp_digitize(const T* __restrict
   if (threadIdx.x == 0) e_s = *(volatile int*)ctl + 1;
   __syncthreads();
   const int e = e_s;
+  // Two halves of slots, by epoch parity: a rank can finish call e (it has every rank's call-e words) and write its
+  // call e + 1 words before a slower rank has read call e's; they land in the other half. It cannot get to call
+  // e + 2 (the same half again) before every rank has written its call e + 1 words, i.e. has finished call e.
+  const int half = e & 1;
   // 1. maxima of this rank's slice of each row, to slot [rank][row] of every rank
   for (int row = blockIdx.x; row < rows; row += gridDim.x) {
     const T* xr = x + (int64_t)row * ldx;
@@ -132,7 +136,7 @@ __global__ void __launch_bounds__(DIG_THREADS) k_tp_digitize(const T* __restrict
     amax = block_max(amax, redf);
     if ((int)threadIdx.x < world) {
       const unsigned long long w = ((unsigned long long)(uint32_t)e << 32) | __float_as_uint(amax);
-      st_relaxed_sys_u64(xch[threadIdx.x] + (int64_t)rank * max_rows + row, w);
+      st_relaxed_sys_u64(xch[threadIdx.x] + ((int64_t)half * world + rank) * max_rows + row, w);
     }
     __syncthreads();  // redf is reused by the next row's reduction
   }
@@ -141,7 +145,7 @@ __global__ void __launch_bounds__(DIG_THREADS) k_tp_digitize(const T* __restrict
     if (threadIdx.x < 32) {
       float v = 0.0f;
       if ((int)threadIdx.x < world)
-        v = __uint_as_float(tpf_wait_word(xch[rank] + (int64_t)threadIdx.x * max_rows + row, e));
+        v = __uint_as_float(tpf_wait_word(xch[rank] + ((int64_t)half * world + threadIdx.x) * max_rows + row, e));
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
       if (threadIdx.x == 0) gmax_s = v;

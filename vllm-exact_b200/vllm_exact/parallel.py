@@ -150,7 +150,7 @@ class PeerRowParallel:
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.device = dev
         self.max_rows, self.max_cols = max_rows, max_cols
-        self.xch = torch.zeros(self.world * max_rows, dtype=torch.int64, device=dev)  # (epoch, max) words
+        self.xch = torch.zeros(2 * self.world * max_rows, dtype=torch.int64, device=dev)  # (epoch, max) words
         self.part = torch.zeros(max_rows * max_cols, dtype=torch.int64, device=dev)
         self.outx = torch.zeros(max_rows * max_cols, dtype=torch.int64, device=dev)  # epoch words (fp32: one each)
         self.flags = torch.zeros(_lib.tp_flag_words(self.world), dtype=torch.int32, device=dev)
