@@ -508,7 +508,11 @@ def run_tp(args, dev, rank, world, local):
         if name in ROW_PARALLEL:
             # the peer path's three launches, each timed alone (10 back to back per graph): maxima exchange +
             # digitize, partial GEMM into the shared buffer, reduce-scatter + epilogue + all-gather
-            xd = peer.digitize(XS[(M, name)], 14)
+            # every call of the peer object on this rank goes to one stream: two of its kernels overlapping on the GPU
+            # would read the same call epoch and leave this rank's epochs out of step with the other ranks'
+            with torch.cuda.stream(stream):
+                xd = peer.digitize(XS[(M, name)], 14)
+            torch.cuda.synchronize()
             part = peer.partial(M, N)
             parts = {}
             for step_name, fn in (("exchange_digitize", lambda: peer.digitize(XS[(M, name)], 14, out=xd)),

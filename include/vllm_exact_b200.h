@@ -183,7 +183,8 @@ int ex_ipc_close_handle(void* base);
  * The two exchange steps of a row-parallel (K-sharded) layer over peer memory, one kernel each (replacing the MAX
  * all-reduce of row maxima + ex_digitize_given_absmax, and the int64 SUM all-reduce of the partial totals +
  * ex_epilogue_i64). Every rank of the group makes the same calls in the same order; ranks run on different GPUs (the
- * kernels wait for one another). Buffers named "of every rank" are device arrays of `world` pointers, index p = rank
+ * kernels wait for one another), and on one rank calls sharing a ctl array must not overlap on the GPU (each reads
+ * its call epoch from ctl). Buffers named "of every rank" are device arrays of `world` pointers, index p = rank
  * p's buffer as mapped on this GPU (e.g. with ex_ipc_open_handle), this rank's at index `rank`; all of them are
  * zero-filled once before the first call. Values cross GPUs as 64-bit words (call epoch << 32 | payload) that the
  * reader polls, so no fence is needed. Epochs live in the ctl words on the device, so calls can be captured in a CUDA

@@ -138,8 +138,10 @@ class PeerRowParallel:
     objects). Between the two runs the partial GEMM, written straight into this rank's shared partial buffer.
 
     One object per process group and largest call (max_rows x max_cols outputs). Same arguments and bitwise the same
-    result as row_parallel_linear. Calls must be issued in the same order on every rank of the group; the epochs live
-    on the device, so calls can be captured in CUDA graphs."""
+    result as row_parallel_linear. Calls must be issued in the same order on every rank of the group, and on one rank
+    they must not overlap on the GPU (issue them on one stream, or order the streams): each kernel reads its call
+    epoch from the device, so two overlapping calls would take the same epoch and leave this rank out of step with
+    the others. The epochs live on the device, so calls can be captured in CUDA graphs."""
 
     def __init__(self, max_rows: int, max_cols: int, group=None, device=None):
         g = group if group is not None else _default_group()
