@@ -389,7 +389,7 @@ def run_tp(args, dev, rank, world, local):
     give the 1-GPU bits."""
     import torch
     import torch.distributed as dist
-    from vllm_exact import kernels as KK, parallel as P
+    from vllm_exact import _lib, kernels as KK, parallel as P
     g = dist.group.WORLD
     hbm, _, _, peak_kind = peaks()
     W = tp_shards(rank, world, dev)
@@ -575,6 +575,9 @@ def run_tp(args, dev, rank, world, local):
                  "first_mismatch": r["first_mismatch"],
                  "sample": "every rank: rows {0, M-1} of each of its 15 layer outputs x all its output columns vs the "
                            "CPU oracle of the unsharded layer (bf16 bits)"}
+    # a bounded wait in a peer kernel that ran out anywhere above sets the device error word: reported, max over ranks
+    derr = torch.tensor([_lib.device_error()], dtype=torch.int64, device=dev)
+    dist.all_reduce(derr, op=dist.ReduceOp.MAX)
     launches = sum((3 if best == "peer" else 4) if name in ROW_PARALLEL else 2 for M, name, K, N in order)
     result = {
         "metric": METRIC, "value": round(value, 4), "unit": "TB/s", "n_gpus": world, "steps": args.steps,
@@ -605,7 +608,7 @@ def run_tp(args, dev, rank, world, local):
                 "api": "kernels.exact_linear / the row-parallel path above, per rank, pinned host in and out inside "
                        "one CUDA graph per step, max over ranks"},
         "per_layer_us": per_layer, "collectives_us": coll,
-        "bitwise": check, "bitwise_ok": check["ok"],
+        "bitwise": check, "bitwise_ok": check["ok"], "device_error": int(derr),
     }
     del gS
     torch.cuda.synchronize()

@@ -204,6 +204,16 @@ def _worker_peer(rank, world, port, root, q):
         torch.cuda.synchronize()
         res["digitize_back_to_back"] = (all(torch.equal(o[0], ref[0]) and torch.equal(o[1], ref[1]) and
                                             torch.equal(o[3], ref[3]) for o in outs), True)
+        # the same calls alternating between two streams with nothing ordering them: the object orders each call
+        # after the previous one, so no two take the same epoch
+        sts = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+        outs = []
+        for i in range(12):
+            with torch.cuda.stream(sts[i % 2]):
+                outs.append(peer.digitize(xs, 14))
+        torch.cuda.synchronize()
+        res["digitize_two_streams"] = (all(torch.equal(o[0], ref[0]) and torch.equal(o[1], ref[1]) and
+                                           torch.equal(o[3], ref[3]) for o in outs), True)
         torch.cuda.synchronize()
         code = ctypes_code()
         q.put((rank, res, code))

@@ -139,9 +139,10 @@ class PeerRowParallel:
 
     One object per process group and largest call (max_rows x max_cols outputs). Same arguments and bitwise the same
     result as row_parallel_linear. Calls must be issued in the same order on every rank of the group, and on one rank
-    they must not overlap on the GPU (issue them on one stream, or order the streams): each kernel reads its call
-    epoch from the device, so two overlapping calls would take the same epoch and leave this rank out of step with
-    the others. The epochs live on the device, so calls can be captured in CUDA graphs."""
+    they must not overlap on the GPU: each kernel reads its call epoch from the device, so two overlapping calls would
+    take the same epoch and leave this rank out of step with the others. A call issued on another stream than the
+    previous one is made to wait for that stream; inside graph capture the capturing stream must order them. The
+    epochs live on the device, so calls can be captured in CUDA graphs."""
 
     def __init__(self, max_rows: int, max_cols: int, group=None, device=None):
         g = group if group is not None else _default_group()
@@ -173,6 +174,15 @@ class PeerRowParallel:
             torch.tensor([ptrs[p][k] for p in range(self.world)], dtype=torch.int64, device=dev) for k in range(4))
         torch.cuda.synchronize(dev)
         dist.barrier(group=g)  # every rank has mapped every buffer before the first call
+        self._last_stream = None
+
+    def _ordered(self, dev) -> None:
+        """Order this call after the previous one when it is issued on another stream (outside graph capture, where
+        the capturing stream orders the calls): two calls overlapping on the GPU would take the same epoch."""
+        s = torch.cuda.current_stream(dev)
+        if self._last_stream is not None and s != self._last_stream and not torch.cuda.is_current_stream_capturing():
+            s.wait_stream(self._last_stream)
+        self._last_stream = s
 
     def _handle(self, t: torch.Tensor):
         """(handle of the allocation holding t, byte offset of t inside it)."""
@@ -209,6 +219,7 @@ class PeerRowParallel:
             raise ValueError(f"PeerRowParallel holds {self.max_rows} rows, the call has {M}")
         dev = x2.device
         h, l, cs, sh = out if out is not None else K._alloc_digits(M, Kd, dev)
+        self._ordered(dev)
         with torch.cuda.device(dev):
             check("ex_tp_digitize",
                   lib().ex_tp_digitize(x2.data_ptr(), K._DT[x2.dtype], x2.stride(0), M, Kd, F,
@@ -228,6 +239,7 @@ class PeerRowParallel:
         """Step 3 (ex_allreduce_epilogue_i64): the partials every rank wrote into its partial(M, N) summed, scaled
         and written to `out` (M x N, row-major, bf16/fp16/fp32)."""
         dev = out.device
+        self._ordered(dev)
         with torch.cuda.device(dev):
             check("ex_allreduce_epilogue_i64",
                   lib().ex_allreduce_epilogue_i64(self.part_ptrs.data_ptr(), N, self.outx_ptrs.data_ptr(),
