@@ -410,7 +410,7 @@ def run_tp(args, dev, rank, world, local):
             KK.lib().ex_linear_workspace_bytes(M, N // world, K, 0, 0)
     KK.reserve_workspace(max(ws_need(*o) for o in order), dev, stream=stream)
 
-    peer = P.PeerRowParallel(max(DECODE_M), max(N for name, K, N in SHAPES if name in ROW_PARALLEL), group=g)
+    peer = P.PeerRowParallel(256, max(N for name, K, N in SHAPES if name in ROW_PARALLEL), group=g)
 
     def layer(M, name, path="peer"):
         if name not in ROW_PARALLEL:
@@ -524,6 +524,23 @@ def run_tp(args, dev, rank, world, local):
                 del gl
             row["peer_launches"] = parts
         per_layer[f"{name}/M{M}"] = row if name in ROW_PARALLEL else row["peer"]
+    # the row-parallel layers at M = 256 (the b256 decode batch), both paths, and whether they give the same bits
+    for i, (name, K, N) in enumerate(SHAPES):
+        if name not in ROW_PARALLEL:
+            continue
+        ks = K // world
+        xs = make_activation(256, K, 9000 + i, dev)[:, rank * ks:(rank + 1) * ks].contiguous()
+        ys = {path: torch.empty(256, N, device=dev, dtype=torch.bfloat16) for path in ("peer", "nccl")}
+        fns = {"peer": lambda: peer.linear(xs, *W[name], 14, True, out=ys["peer"]),
+               "nccl": lambda: P.row_parallel_linear(xs, *W[name], 14, True, group=g, out=ys["nccl"])}
+        row = {}
+        for path in ("peer", "nccl"):
+            gl = graph_of(lambda: [fns[path]() for _ in range(10)])
+            row[path] = round(timed(gl, 5) * 100, 2)
+            del gl
+        torch.cuda.synchronize()
+        row["same_bits"] = bool(torch.equal(ys["peer"], ys["nccl"]))
+        per_layer[f"{name}/M256"] = row
     for M in DECODE_M:
         amax = torch.ones(M, device=dev)
         tot = torch.zeros(M, 4096, dtype=torch.int64, device=dev)
@@ -1157,13 +1174,16 @@ def engine_case(args):
     and temperature 1.0 (top-k 20, top-p 0.95, per-request seeds), tokens and logprobs compared bitwise; speed =
     (t(321 new tokens) - t(65 new tokens)) / 256 with the minimum of two runs each, at (256, 1K), (64, 8K), (16, 16K),
     prompt lengths uniform in [0.75, 1.25] x ctx. Prints one JSON line. One arm per process. Options after the arm:
-    `tp=N` (tensor-parallel size), `layers=L` (default 32), `inv` (invariance only, no speed runs)."""
+    `tp=N` (tensor-parallel size), `layers=L` (default 32), `inv` (invariance only, no speed runs), `peer=R` (row-
+    parallel calls of up to R rows over peer memory, 0 = NCCL only; default the package's setting)."""
     import random
     import time
     parts = args.case.split(":")
     arm = parts[1] if len(parts) > 1 else "exact"
     opts = dict(o.split("=") if "=" in o else (o, "1") for o in parts[2:])
     tp, layers, inv_only = int(opts.get("tp", 1)), int(opts.get("layers", 32)), opts.get("inv") == "1"
+    if "peer" in opts:  # read by vllm_exact.parallel on import, in this process and in the tensor-parallel workers
+        os.environ["VLLM_EXACT_B200_PEER_ROWS"] = opts["peer"]
     kw = {}
     if arm == "exact":
         import vllm_exact
@@ -1181,6 +1201,8 @@ def engine_case(args):
               tensor_parallel_size=tp, **kw)
     res = {"arm": arm, "tp": tp, "layers": layers, "startup_s": round(time.time() - t0, 1), "invariance": {},
            "speed": {}}
+    if arm == "exact" and tp > 1:
+        res["peer_rows"] = int(os.environ.get("VLLM_EXACT_B200_PEER_ROWS", "256"))
 
     def prompts_of(n, lo, hi, seed):
         rng = random.Random(seed)

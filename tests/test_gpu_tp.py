@@ -214,6 +214,25 @@ def _worker_peer(rank, world, port, root, q):
         torch.cuda.synchronize()
         res["digitize_two_streams"] = (all(torch.equal(o[0], ref[0]) and torch.equal(o[1], ref[1]) and
                                            torch.equal(o[3], ref[3]) for o in outs), True)
+        # the plugin's op: the group's peer object made once (as the plugin does at load time), then calls of up to
+        # PEER_ROWS rows over peer memory and larger ones through NCCL, all equal to the 1-GPU layer
+        from vllm_exact import ops  # noqa: F401  (registers exactmm::linear_row_parallel)
+        auto = P.peer_for(dev, dist.group.WORLD, create=True)
+        Kd, N = 4096, 1024
+        ks = Kd // world
+        a, b = rank * ks, (rank + 1) * ks
+        w = (torch.randn(N, Kd, generator=torch.Generator().manual_seed(21)) * 0.02).bfloat16().to(dev)
+        wd_full = K.digitize(w, 14)
+        wd = P.digitize_weight_row_sharded(w[:, a:b].contiguous(), 14)
+        for M in (3, P.PEER_ROWS, P.PEER_ROWS + 5):
+            x = torch.randn(M, Kd, generator=torch.Generator().manual_seed(M)).bfloat16().to(dev)
+            ref = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            K.exact_linear(K.digitize(x, 14), wd_full, 14, True, out=ref)
+            y = torch.ops.exactmm.linear_row_parallel(x[:, a:b], *wd)
+            res[f"op_M{M}"] = (auto is not None and bool(torch.equal(y, ref)), True)
+        torch.cuda.synchronize()
+        if auto is not None:
+            auto.close()
         torch.cuda.synchronize()
         code = ctypes_code()
         q.put((rank, res, code))

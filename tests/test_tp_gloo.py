@@ -78,3 +78,56 @@ def test_row_parallel_two_ranks_bitexact():
         assert p.exitcode == 0
     for r in range(2):
         assert all(res[r].values()), res[r]
+
+
+def _worker_peer_agreement(rank, world, port, root, result_q):
+    """parallel.peer_for on 2 CPU ranks with the device steps of PeerRowParallel faked: a failure on one rank (no IPC
+    handle, or a peer mapping that cannot be opened) gives None on every rank, success gives an object on every rank,
+    and asking again takes no collective step."""
+    import datetime
+    import sys
+    for p in (root, os.path.join(root, "vllm-exact_b200")):
+        sys.path.insert(0, p)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    try:
+        from vllm_exact import _lib, parallel as Par
+        torch.cuda.synchronize = lambda *a, **k: None  # no device here: the buffers are CPU tensors
+        out = {}
+        for case in ("handle_fails", "open_fails", "ok"):
+            def handle(self, t, case=case):
+                if case == "handle_fails" and rank == 1:
+                    raise _lib.ExactError("ex_ipc_get_handle", 1, "faked")
+                return (b"h%d" % rank, 0)
+
+            def open_(self, h, case=case):
+                if case == "open_fails" and rank == 1:
+                    raise _lib.ExactError("ex_ipc_open_handle", 1, "faked")
+                return 4096
+
+            Par.PeerRowParallel._handle, Par.PeerRowParallel._open = handle, open_
+            Par._PEERS.clear()
+            g = dist.group.WORLD
+            first = Par.peer_for("cpu", g, create=True)
+            again = Par.peer_for("cpu", g, create=True)  # cached: no collective step (a lone one would time out)
+            out[case] = (first is not None, again is first)
+        dist.barrier()
+        result_q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_path_made_on_every_rank_or_none():
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_peer_agreement, args=(r, 2, port, root, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(2):
+        assert res[r] == {"handle_fails": (False, True), "open_fails": (False, True), "ok": (True, True)}, res[r]

@@ -6,8 +6,9 @@ processed in blocks of RB (rows are independent, so the block size never changes
 library: digitize, then the exact GEMM with fused epilogue.
 
 ``exactmm::linear_row_parallel`` (no reference counterpart: the reference runs on one GPU): the same for a K-sharded
-(row-parallel) layer of a tensor-parallel group, x being this rank's K slice; the exchange steps of
-parallel.row_parallel_linear run inside the op, so torch.compile sees one opaque call, as for the 1-GPU op.
+(row-parallel) layer of a tensor-parallel group, x being this rank's K slice; the exchange steps (over peer memory
+for calls of up to parallel.PEER_ROWS rows, else NCCL; bitwise the same) run inside the op, so torch.compile sees one
+opaque call, as for the 1-GPU op.
 
 F and TRUNC are set by vllm_exact.enable().
 """
@@ -51,8 +52,10 @@ def exact_linear_row_parallel_op(x: torch.Tensor, wh: torch.Tensor, wl: torch.Te
     x2 = x.reshape(-1, shp[-1])
     M = x2.shape[0]
     out = x.new_empty(M, N)
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
     for i in range(0, M, RB):  # every rank holds the same rows, so every rank makes the same collective calls
-        parallel.row_parallel_linear(x2[i:i + RB], wh, wl, cw, sw, F, TRUNC, out=out[i:i + RB])
+        parallel.row_parallel_linear_auto(x2[i:i + RB], wh, wl, cw, sw, F, TRUNC, out=out[i:i + RB])
     return out.reshape(*shp[:-1], N)
 
 

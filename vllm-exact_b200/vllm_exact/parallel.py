@@ -24,6 +24,7 @@ exercise the collective logic on CPU ranks (gloo), the way a fake device layer i
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 import torch.distributed as dist
@@ -74,6 +75,46 @@ def _default_group():
         return get_tp_group().device_group
     except Exception:
         return dist.group.WORLD
+
+
+# Row-parallel calls of at most PEER_ROWS rows and PEER_COLS (even) output columns go through a PeerRowParallel object
+# of their (device, group) where one exists; larger calls, and groups where peer memory is unavailable, take the NCCL
+# path (bitwise the same results). VLLM_EXACT_B200_PEER_ROWS=0 turns the peer path off.
+PEER_ROWS = int(os.environ.get("VLLM_EXACT_B200_PEER_ROWS", "256"))
+PEER_COLS = 16384
+_PEERS = {}  # (device index, group) -> PeerRowParallel, or None where it could not be made
+
+
+def peer_for(device, group=None, create: bool = False):
+    """The PeerRowParallel object of (device, group), or None. With create=True it is made on first request: that is
+    a collective step, so every rank of the group must ask at the same point of its program, outside CUDA graph
+    capture (the plugin asks while loading the weights of its first row-parallel layer). If the peer mappings fail on
+    any rank, every rank records None and keeps the NCCL path."""
+    g = group if group is not None else _default_group()
+    dev = torch.device(device)
+    key = (dev.index, g)
+    if key in _PEERS or not create:
+        return _PEERS.get(key)
+    if PEER_ROWS <= 0 or dist.get_world_size(g) < 2:
+        _PEERS[key] = None
+        return None
+    try:
+        _PEERS[key] = PeerRowParallel(PEER_ROWS, PEER_COLS, group=g, device=dev)
+    except RuntimeError:
+        _PEERS[key] = None
+    return _PEERS[key]
+
+
+def row_parallel_linear_auto(x2: torch.Tensor, wh, wl, cw, sw, F: int, trunc: bool, out: torch.Tensor,
+                             group=None) -> torch.Tensor:
+    """One row-parallel call (x2: M x K_local rows with unit column stride, out: M x N): over peer memory when the
+    (device, group) has a PeerRowParallel object and the call fits it, else row_parallel_linear. The choice depends
+    only on shapes and on objects made at the same point on every rank, so every rank takes the same path."""
+    peer = peer_for(x2.device, group)
+    M, N = x2.shape[0], wh.shape[0]
+    if peer is not None and M <= peer.max_rows and N <= peer.max_cols and N % 2 == 0 and out.stride(0) % 2 == 0:
+        return peer.linear(x2, wh, wl, cw, sw, F, trunc, out=out)
+    return row_parallel_linear(x2, wh, wl, cw, sw, F, trunc, group=group, out=out)
 
 
 def global_row_absmax(x: torch.Tensor, group=None, ops=CudaOps) -> torch.Tensor:
@@ -153,28 +194,43 @@ class PeerRowParallel:
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.device = dev
         self.max_rows, self.max_cols = max_rows, max_cols
-        self.xch = torch.zeros(2 * self.world * max_rows, dtype=torch.int64, device=dev)  # (epoch, max) words
-        self.part = torch.zeros(max_rows * max_cols, dtype=torch.int64, device=dev)
-        self.outx = torch.zeros(max_rows * max_cols, dtype=torch.int64, device=dev)  # epoch words (fp32: one each)
-        self.flags = torch.zeros(_lib.tp_flag_words(self.world), dtype=torch.int32, device=dev)
-        self.ctl = torch.zeros(4, dtype=torch.int32, device=dev)  # [0:2] ex_tp_digitize, [2:4] the all-reduce
-        torch.cuda.synchronize(dev)
-        mine = [self._handle(t) for t in (self.xch, self.part, self.outx, self.flags)]
-        every = [None] * self.world
-        dist.all_gather_object(every, mine, group=g)
         self._opened = []
         self._bases = {}  # exported allocation handle -> mapped base (tensors may share one allocation)
-        ptrs = []  # ptrs[p] = device addresses of rank p's buffers, as seen from this GPU
-        for p, hs in enumerate(every):
-            if p == self.rank:
-                ptrs.append([t.data_ptr() for t in (self.xch, self.part, self.outx, self.flags)])
-            else:
-                ptrs.append([self._open(h) + off for h, off in hs])
-        self.xch_ptrs, self.part_ptrs, self.outx_ptrs, self.flag_ptrs = (
-            torch.tensor([ptrs[p][k] for p in range(self.world)], dtype=torch.int64, device=dev) for k in range(4))
-        torch.cuda.synchronize(dev)
-        dist.barrier(group=g)  # every rank has mapped every buffer before the first call
         self._last_stream = None
+        # Every rank takes the same two collective steps whatever fails locally, so a failure on one rank raises on
+        # all of them (no rank left waiting in a collective, none left with a half-made object).
+        try:
+            self.xch = torch.zeros(2 * self.world * max_rows, dtype=torch.int64, device=dev)  # (epoch, max) words
+            self.part = torch.zeros(max_rows * max_cols, dtype=torch.int64, device=dev)
+            self.outx = torch.zeros(max_rows * max_cols, dtype=torch.int64, device=dev)  # epoch words (fp32: one each)
+            self.flags = torch.zeros(_lib.tp_flag_words(self.world), dtype=torch.int32, device=dev)
+            self.ctl = torch.zeros(4, dtype=torch.int32, device=dev)  # [0:2] ex_tp_digitize, [2:4] the all-reduce
+            torch.cuda.synchronize(dev)
+            mine = [self._handle(t) for t in (self.xch, self.part, self.outx, self.flags)]
+        except RuntimeError:  # out of memory, or no IPC handle for the allocation
+            mine = None
+        every = [None] * self.world
+        dist.all_gather_object(every, mine, group=g)
+        ok = all(hs is not None for hs in every)
+        if ok:
+            try:
+                ptrs = []  # ptrs[p] = device addresses of rank p's buffers, as seen from this GPU
+                for p, hs in enumerate(every):
+                    if p == self.rank:
+                        ptrs.append([t.data_ptr() for t in (self.xch, self.part, self.outx, self.flags)])
+                    else:
+                        ptrs.append([self._open(h) + off for h, off in hs])
+                self.xch_ptrs, self.part_ptrs, self.outx_ptrs, self.flag_ptrs = (
+                    torch.tensor([ptrs[p][k] for p in range(self.world)], dtype=torch.int64, device=dev)
+                    for k in range(4))
+                torch.cuda.synchronize(dev)
+            except RuntimeError:
+                ok = False
+        oks = [None] * self.world
+        dist.all_gather_object(oks, ok, group=g)  # also: every rank has mapped every buffer before the first call
+        if not all(oks):
+            self.close()
+            raise RuntimeError("peer memory between the ranks of the group is not available on every rank")
 
     def _ordered(self, dev) -> None:
         """Order this call after the previous one when it is issued on another stream (outside graph capture, where
@@ -205,6 +261,9 @@ class PeerRowParallel:
 
     def close(self) -> None:
         """Unmap the peers' buffers (after the last call has completed on every rank)."""
+        if not self._opened:
+            self._bases = {}
+            return
         with torch.cuda.device(self.device):
             for p in self._opened:
                 lib().ex_ipc_close_handle(p)

@@ -8,7 +8,8 @@ vllm_exact.enable().
 Tensor parallelism: column-parallel layers (output-sharded: QKV, gate_up, GDN in_proj, vocab-parallel lm_head) hold
 full-K weight rows, so they need nothing special. Row-parallel layers (K-sharded: o_proj, down, GDN out_proj) go
 through parallel.py: global row scales (a MAX all-reduce of row maxima), an exact int64 partial GEMM on the local K
-slice, an int64 SUM all-reduce (exact under any reduction order) and the scaling epilogue. vLLM's own bf16
+slice, an int64 SUM all-reduce (exact under any reduction order) and the scaling epilogue; decode-sized calls run
+both exchanges as peer-memory kernels (parallel.PeerRowParallel), larger ones through NCCL. vLLM's own bf16
 all-reduce of that layer is switched off, because a sum of rounded partials is neither exact nor order-invariant.
 """
 import json
@@ -57,6 +58,9 @@ def _digitize_layer(layer):
     if _is_row_sharded(layer):
         from . import parallel
         h, l, cs, sh = parallel.digitize_weight_row_sharded(w, F)
+        # the peer-memory exchange buffers of the group, made by the first row-parallel layer on every rank (a
+        # collective step at the same point of every rank's loading, outside graph capture)
+        parallel.peer_for(w.device, create=True)
     else:
         h, l, cs, sh = K.digitize_weight(w, F)
     layer.register_buffer("ex_wh", h, persistent=False)
