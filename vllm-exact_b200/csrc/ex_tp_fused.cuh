@@ -14,8 +14,8 @@
 //   -> whole-row maxima -> digits of the slice. Safe for back-to-back calls on its own (two halves by epoch parity).
 // k_tp_allreduce_epilogue: reduce-scatter + exact epilogue + all-gather of the int64 partial totals. Rank r owns the
 //   output columns [r N / p, (r + 1) N / p) (rounded down to even): after one flag exchange saying every rank's
-//   partial is complete (one thread per peer), it sums the p partials of its columns (the p peer loads of a column
-//   pair issued together; integer addition is exact in any order),
+//   partial is complete (one thread per peer), it sums the p partials of its columns (the peer loads of a column
+//   pair issued four ranks at a time; integer addition is exact in any order),
 //   applies the epilogue once, and stores the finished values as epoch words into every rank's output exchange buffer
 //   (a bf16/fp16 column pair or one fp32 value per word). Each block then copies into `out` the words of its share of
 //   every rank's columns, waiting for each word's epoch. Block b of every rank covers the same positions, so a block
@@ -37,6 +37,7 @@ namespace ex {
 constexpr int TPF_THREADS = 256;
 constexpr int TPF_MAX_BLOCKS = EX_TP_MAX_BLOCKS;  // blocks of k_tp_allreduce_epilogue
 constexpr int TPF_MAX_WORLD = EX_TP_MAX_WORLD;
+constexpr int TPF_LOAD_GROUP = 4;  // peer loads issued together by one thread of k_tp_allreduce_epilogue
 
 __device__ __forceinline__ void st_release_sys(int* p, int v) {
   asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -222,9 +223,6 @@ __global__ void __launch_bounds__(TPF_THREADS) k_tp_allreduce_epilogue(
   const bool ok = __syncthreads_and(ok_t) != 0;
   const unsigned long long tag = (unsigned long long)(uint32_t)e << 32;
   if (ok) {
-    const long long* part_of[TPF_MAX_WORLD];
-#pragma unroll
-    for (int p = 0; p < TPF_MAX_WORLD; ++p) part_of[p] = p < world ? parts[p] : nullptr;
     // 1. this rank's columns: block b takes pairs [b * P / B, (b + 1) * P / B) of the M x (c1 - c0) / 2 pairs
     const int c0 = tpf_col0(rank, N, world), c1 = tpf_col0(rank + 1, N, world);
     const int half = (c1 - c0) >> 1;
@@ -233,18 +231,21 @@ __global__ void __launch_bounds__(TPF_THREADS) k_tp_allreduce_epilogue(
     for (int64_t i = p0 + threadIdx.x; i < p1; i += TPF_THREADS) {
       const int m = (int)(i / half), n = c0 + 2 * (int)(i % half);
       const int64_t off = (int64_t)m * ldt + n;
-      // every rank's pair loaded before any is used: the world peer loads are in flight together
-      longlong2 v[TPF_MAX_WORLD];
-#pragma unroll
-      for (int p = 0; p < TPF_MAX_WORLD; ++p)
-        if (p < world) v[p] = ld_relaxed_sys_v2s64(part_of[p] + off);
+      // the pairs of TPF_LOAD_GROUP ranks loaded before any is used, so that many peer loads are in flight together
+      // (few registers: this kernel's blocks must fit beside the partial GEMM's CTAs, which launch it early)
       long long t0 = 0, t1 = 0;
+      for (int g = 0; g < world; g += TPF_LOAD_GROUP) {
+        longlong2 v[TPF_LOAD_GROUP];
 #pragma unroll
-      for (int p = 0; p < TPF_MAX_WORLD; ++p)
-        if (p < world) {
-          t0 += v[p].x;
-          t1 += v[p].y;
-        }
+        for (int j = 0; j < TPF_LOAD_GROUP; ++j)
+          if (g + j < world) v[j] = ld_relaxed_sys_v2s64(parts[g + j] + off);
+#pragma unroll
+        for (int j = 0; j < TPF_LOAD_GROUP; ++j)
+          if (g + j < world) {
+            t0 += v[j].x;
+            t1 += v[j].y;
+          }
+      }
       const int sxm = sx[m];
       const float f0 = ex_scale_to_f32(t0, sxm, sw[n]), f1 = ex_scale_to_f32(t1, sxm, sw[n + 1]);
       if constexpr (F32) {
