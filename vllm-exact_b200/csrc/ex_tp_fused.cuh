@@ -14,8 +14,7 @@
 //   -> whole-row maxima -> digits of the slice. Safe for back-to-back calls on its own (two halves by epoch parity).
 // k_tp_allreduce_epilogue: reduce-scatter + exact epilogue + all-gather of the int64 partial totals. Rank r owns the
 //   output columns [r N / p, (r + 1) N / p) (rounded down to even): after one flag exchange saying every rank's
-//   partial is complete (one thread per peer), it sums the p partials of its columns (the peer loads of a column
-//   pair issued four ranks at a time; integer addition is exact in any order),
+//   partial is complete, it sums the p partials of its columns (peer loads; integer addition is exact in any order),
 //   applies the epilogue once, and stores the finished values as epoch words into every rank's output exchange buffer
 //   (a bf16/fp16 column pair or one fp32 value per word). Each block then copies into `out` the words of its share of
 //   every rank's columns, waiting for each word's epoch. Block b of every rank covers the same positions, so a block
@@ -37,7 +36,6 @@ namespace ex {
 constexpr int TPF_THREADS = 256;
 constexpr int TPF_MAX_BLOCKS = EX_TP_MAX_BLOCKS;  // blocks of k_tp_allreduce_epilogue
 constexpr int TPF_MAX_WORLD = EX_TP_MAX_WORLD;
-constexpr int TPF_LOAD_GROUP = 4;  // peer loads issued together by one thread of k_tp_allreduce_epilogue
 
 __device__ __forceinline__ void st_release_sys(int* p, int v) {
   asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -206,23 +204,23 @@ __global__ void __launch_bounds__(TPF_THREADS) k_tp_allreduce_epilogue(
     int* const* __restrict__ flags, int* ctl, int rank, int world, const int32_t* __restrict__ sx,
     const int32_t* __restrict__ sw, int M, int N, void* __restrict__ out, int64_t ldo) {
   constexpr bool F32 = OUT_DTYPE == EX_DTYPE_F32;
-  __shared__ int e_s;
+  __shared__ int e_s, ok_s;
   const int b = blockIdx.x, B = gridDim.x;
   pdl_launch_dependents();
   pdl_wait();  // this rank's partial comes from the previous kernel (the partial GEMM)
-  if (threadIdx.x == 0) e_s = *(volatile int*)ctl + 1;
+  if (threadIdx.x == 0) {
+    const int e = *(volatile int*)ctl + 1;
+    e_s = e;
+    // announce this rank's partial to every rank (every block stores the same value), then wait for every rank's
+    for (int p = 0; p < world; ++p) st_release_sys(flags[p] + rank, e);
+    int ok = 1;
+    for (int p = 0; p < world && ok; ++p) ok = tpf_wait_flag(flags[rank] + p, e) ? 1 : 0;
+    ok_s = ok;
+  }
   __syncthreads();
   const int e = e_s;
-  // thread t < world announces this rank's partial to rank t (every block stores the same value) and waits for rank
-  // t's: the world flag round trips run side by side
-  int ok_t = 1;
-  if (threadIdx.x < world) {
-    st_release_sys(flags[threadIdx.x] + rank, e);
-    ok_t = tpf_wait_flag(flags[rank] + threadIdx.x, e) ? 1 : 0;
-  }
-  const bool ok = __syncthreads_and(ok_t) != 0;
   const unsigned long long tag = (unsigned long long)(uint32_t)e << 32;
-  if (ok) {
+  if (ok_s) {
     // 1. this rank's columns: block b takes pairs [b * P / B, (b + 1) * P / B) of the M x (c1 - c0) / 2 pairs
     const int c0 = tpf_col0(rank, N, world), c1 = tpf_col0(rank + 1, N, world);
     const int half = (c1 - c0) >> 1;
@@ -231,20 +229,11 @@ __global__ void __launch_bounds__(TPF_THREADS) k_tp_allreduce_epilogue(
     for (int64_t i = p0 + threadIdx.x; i < p1; i += TPF_THREADS) {
       const int m = (int)(i / half), n = c0 + 2 * (int)(i % half);
       const int64_t off = (int64_t)m * ldt + n;
-      // the pairs of TPF_LOAD_GROUP ranks loaded before any is used, so that many peer loads are in flight together
-      // (few registers: this kernel's blocks must fit beside the partial GEMM's CTAs, which launch it early)
       long long t0 = 0, t1 = 0;
-      for (int g = 0; g < world; g += TPF_LOAD_GROUP) {
-        longlong2 v[TPF_LOAD_GROUP];
-#pragma unroll
-        for (int j = 0; j < TPF_LOAD_GROUP; ++j)
-          if (g + j < world) v[j] = ld_relaxed_sys_v2s64(parts[g + j] + off);
-#pragma unroll
-        for (int j = 0; j < TPF_LOAD_GROUP; ++j)
-          if (g + j < world) {
-            t0 += v[j].x;
-            t1 += v[j].y;
-          }
+      for (int p = 0; p < world; ++p) {
+        const longlong2 v = ld_relaxed_sys_v2s64(parts[p] + off);
+        t0 += v.x;
+        t1 += v.y;
       }
       const int sxm = sx[m];
       const float f0 = ex_scale_to_f32(t0, sxm, sw[n]), f1 = ex_scale_to_f32(t1, sxm, sw[n + 1]);
