@@ -111,6 +111,11 @@ def _worker_peer_agreement(rank, world, port, root, result_q):
             first = Par.peer_for("cpu", g, create=True)
             again = Par.peer_for("cpu", g, create=True)  # cached: no collective step (a lone one would time out)
             out[case] = (first is not None, again is first)
+        # the path switched off: no object, no collective step
+        Par._PEERS.clear()
+        rows, Par.PEER_ROWS = Par.PEER_ROWS, 0
+        out["off"] = (Par.peer_for("cpu", dist.group.WORLD, create=True) is not None, True)
+        Par.PEER_ROWS = rows
         dist.barrier()
         result_q.put((rank, out))
     finally:
@@ -130,4 +135,5 @@ def test_peer_path_made_on_every_rank_or_none():
         p.join(timeout=60)
         assert p.exitcode == 0
     for r in range(2):
-        assert res[r] == {"handle_fails": (False, True), "open_fails": (False, True), "ok": (True, True)}, res[r]
+        assert res[r] == {"handle_fails": (False, True), "open_fails": (False, True), "ok": (True, True),
+                          "off": (False, True)}, res[r]

@@ -95,8 +95,8 @@ def peer_for(device, group=None, create: bool = False):
     key = (dev.index, g)
     if key in _PEERS or not create:
         return _PEERS.get(key)
-    if PEER_ROWS <= 0 or dist.get_world_size(g) < 2:
-        _PEERS[key] = None
+    if PEER_ROWS <= 0 or not 2 <= dist.get_world_size(g) <= _lib.EX_TP_MAX_WORLD:
+        _PEERS[key] = None  # off, a single rank, or more ranks than the peer kernels take: NCCL path
         return None
     try:
         _PEERS[key] = PeerRowParallel(PEER_ROWS, PEER_COLS, group=g, device=dev)
