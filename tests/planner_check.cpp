@@ -16,6 +16,7 @@
 // Prints "OK <plans> <segments> <cluster plans>" or the first violation, and exits non-zero on a violation.
 #include <algorithm>
 #include <cstdio>
+#include <string>
 #include <vector>
 
 #include "ex_tc_plan.h"
@@ -114,7 +115,24 @@ bool check_plan(int64_t M, int64_t N, int64_t K, int split_k, int sms, const int
 
 }  // namespace
 
-int main() {
+// `planner_check dump`: the automatic plans of the configs[1] shapes on 148 SMs whose clusters sit in groups of 18 SMs
+// (one line each: M N K BT m_tiles n_tiles KI gs groups chunks G cs ks ws_bytes), for the plan-choice test.
+int dump() {
+  int cap[TC_MAX_CLUSTER + 1] = {};
+  for (int c = 2; c <= TC_MAX_CLUSTER; ++c) cap[c] = (148 / 18) * (18 / c) + (148 % 18) / c;
+  const int64_t shapes[][2] = {{4096, 6144}, {4096, 4096}, {4096, 24576}, {12288, 4096}, {4096, 151936}};
+  for (int64_t M : {1, 16, 64, 256, 4096})
+    for (const auto& kn : shapes) {
+      const TcPlan p = tc_plan(M, kn[1], kn[0], 0, 148, cap);
+      std::printf("%lld %lld %lld %d %d %d %d %d %d %d %d %d %d %zu\n", (long long)M, (long long)kn[1],
+                  (long long)kn[0], p.BT, p.m_tiles, p.n_tiles, p.KI, p.gs, p.groups, p.chunks, p.G, p.cs, p.ks,
+                  p.ws_bytes);
+    }
+  return 0;
+}
+
+int main(int argc, char** argv) {
+  if (argc > 1 && std::string(argv[1]) == "dump") return dump();
   const int64_t Ms[] = {1, 8, 9, 16, 17, 33, 64, 65, 100, 128, 129, 256, 300, 1000, 4096};
   const int64_t Ns[] = {1, 100, 128, 129, 1024, 4096, 6144, 24576, 151936};
   const int64_t Ks[] = {1, 100, 128, 1024, 4096, 12288, 65536};
