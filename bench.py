@@ -9,13 +9,19 @@ value = algorithmic HBM bytes of the 15 GEMMs (weight digits 2NK + weight scales
 scales 4M + bf16 output 2MN) / device time of the step, in TB/s. Weights of one (K, N) are re-used only after the four
 other matrices (>= 1.5 GB) went through the 126 MB L2, so every step streams its weights from HBM.
 
-Also reported (not part of `value`): the tensor-bound sweep M in {256, 4096} as TFLOP/s of executed digit-product
-flops (6 M N K) against the measured bf16 dense peak, the paged decode attention of configs[3], the end-to-end rate
-through the public op with host copies, the CPU oracle on a bounded sample, and the SM clocks during the run.
+Also reported (not part of `value`): per-layer chains of the decode shapes beside the reference's own Triton op on the
+same inputs with a bitwise comparison (`sweep_decode`), the tensor-bound sweep M in {256, 4096} as executed
+digit-product ops (6 M N K) against an INT8 dense peak measured in the run (and the bf16 peak), the paged decode
+attention of configs[3], config 5's hot-path share against cuBLAS bf16 (`decode_step`) and through the real vLLM
+engine (`engine`), the end-to-end rate through the public op with host copies, and the SM clocks during the run.
 
 After the timed region, rank 0 checks the step's outputs bit for bit against the CPU oracle on a row sample
-(`bitwise_ok`), times the reference's own Triton kernels on the same digits (`ref_triton`), and times the reference's
-CPU integer path on a bounded sample (`cpu_baseline`).
+(`bitwise_ok`) and times the reference's CPU integer path on a bounded sample (`cpu_baseline`).
+
+--gpus N > 1 (under torchrun, one rank per GPU) runs the same step tensor-parallel: qkv, gate_up and lm_head
+column-parallel, o_proj and down K-sharded with the exact int64 sum over peer memory or NCCL (the faster of the two),
+every rank's outputs checked against the oracle of the unsharded layers; value = the step's bytes / its time, max
+over ranks (strong scaling).
 
 --impl reference times the reference's own CPU integer path (digitize_torch + exact_linear_torch from its
 kernels.py, installed under baseline/_ref; the numpy restatement in oracle/ only if it is missing) on a bounded
